@@ -1,0 +1,226 @@
+/*
+ * drift_b200.h — C ABI of the B200 emulated-matmul engine.
+ *
+ * The engine reproduces, bit for bit, drift's policy-parameterised matmul
+ * arithmetic: cast to a minifloat format (MiniFloat), per-tensor / MX scaling
+ * (Quant), and the accumulator/order engine (Dot). Every entry point here
+ * replaces a loop of the Java reference that calls those static methods; the
+ * comment above each one cites the Java interface it stands in for (paths are
+ * relative to the reference project's root).
+ *
+ * Conventions
+ *  - Plain C: no C++ or torch types cross this boundary. Sizes are int64_t.
+ *  - Every function returns a drift status (DRIFT_OK == 0). drift_last_error()
+ *    gives the message of the calling thread's most recent failure.
+ *  - Host entry points take HOST pointers (Java MemorySegment / off-heap
+ *    arrays). They copy to the device, run, copy back, and return only when
+ *    the result is in the caller's buffer. They never keep a pointer.
+ *  - *_dev entry points take DEVICE pointers and a cudaStream_t passed as
+ *    void* (NULL = the context's own stream). They are asynchronous unless
+ *    noted.
+ *  - rng_state is the Java Rng.state() long (java/src/main/java/io/drift/fmt/
+ *    Rng.java:29-31). On return it holds the state the Java Rng would hold
+ *    after the same calls, so callers can interleave engine calls with Java
+ *    code that shares the stream.
+ *  - One drift_ctx per host thread. A context owns a CUDA stream and a
+ *    device workspace; it is not safe to use one context from two threads at
+ *    once. Different contexts share nothing.
+ */
+#ifndef DRIFT_B200_H
+#define DRIFT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define DRIFT_OK            0
+/* Bad enum, shape, stride or null pointer; or stochastic rounding that
+ * needed a draw with no rng (java/.../fmt/MiniFloat.java:270-272). */
+#define DRIFT_EINVAL        1
+/* NaN cast into a format with no NaN: Java throws ArithmeticException
+ * (java/.../fmt/MiniFloat.java:157-160). */
+#define DRIFT_ENAN_FINITE   2
+/* A CUDA runtime call failed. */
+#define DRIFT_ECUDA         3
+/* A bounded device-side wait gave up. */
+#define DRIFT_ETIMEOUT      4
+/* A valid policy this engine does not implement yet. */
+#define DRIFT_EUNSUPPORTED  5
+/* Device memory could not be obtained. */
+#define DRIFT_ENOMEM        6
+
+/* ------------------------------------------------ enums (Java ordinals) */
+/* Formats.ALL order (java/.../fmt/Formats.java:20-48). */
+#define DRIFT_FMT_NONE  (-1)   /* NumericPolicy.inputFormat == null: no cast */
+#define DRIFT_E4M3      0
+#define DRIFT_E5M2      1
+#define DRIFT_E2M1      2
+#define DRIFT_E3M2      3
+#define DRIFT_E2M3      4
+#define DRIFT_FP16      5
+#define DRIFT_BF16      6
+#define DRIFT_NUM_FORMATS 7
+
+/* Rounding (java/.../fmt/Rounding.java:14-20). -1 in a policy's grad_rounding
+ * means "same as input_rounding" (NumericPolicy.gradCastRounding). */
+#define DRIFT_ROUND_INHERIT   (-1)
+#define DRIFT_NEAREST_EVEN    0
+#define DRIFT_STOCHASTIC      1
+#define DRIFT_TRUNCATE        2
+
+/* NumericPolicy.Scaling (java/.../kernel/NumericPolicy.java:56-63). */
+#define DRIFT_SCALE_NONE      0
+#define DRIFT_PER_TENSOR      1
+#define DRIFT_MX_BLOCK        2
+
+/* NumericPolicy.Acc (java/.../kernel/NumericPolicy.java:26-41). */
+#define DRIFT_ACC_FP64        0
+#define DRIFT_ACC_FP32        1
+#define DRIFT_ACC_FP16        2
+#define DRIFT_ACC_BF16        3
+
+/* NumericPolicy.Order (java/.../kernel/NumericPolicy.java:44-53). */
+#define DRIFT_SEQUENTIAL      0
+#define DRIFT_REVERSED        1
+#define DRIFT_PAIRWISE        2
+#define DRIFT_BLOCKED         3
+
+/*
+ * NumericPolicy flattened to a POD (java/.../kernel/NumericPolicy.java:58-96).
+ * A Java caller fills it from the policy object; NumericPolicy.Builder and the
+ * named registry stay on the Java side. Formats are DRIFT_* ids or
+ * DRIFT_FMT_NONE; grad_format DRIFT_FMT_NONE with a non-null input format
+ * means "same as input" (NumericPolicy.gradCastFormat), exactly as a null
+ * gradFormat does in Java.
+ */
+typedef struct drift_policy {
+    int32_t input_format;
+    int32_t grad_format;
+    int32_t input_rounding;
+    int32_t grad_rounding;
+    int32_t scaling;
+    int32_t scale_block;     /* MX block length, Builder default 32 */
+    int32_t amax_history;    /* delayed scaling window, 0 = current */
+    int32_t mx_headroom;     /* added to the OCP shared exponent */
+    int32_t acc;
+    int32_t order;
+    int32_t acc_block;       /* BLOCKED chunk length, Builder default 32 */
+    int32_t acc_rounding;
+    int32_t master_fp32;
+    int32_t cast_scores;
+    int32_t cast_probs;
+    int32_t reserved;        /* must be 0 */
+} drift_policy;
+
+typedef struct drift_ctx drift_ctx;
+
+/* ------------------------------------------------------------ lifecycle */
+/* Opens a context on CUDA device `device` with its own stream. */
+int drift_open(int device, drift_ctx **out);
+int drift_close(drift_ctx *ctx);
+/* Message for the calling thread's most recent non-OK status. */
+const char *drift_last_error(void);
+/* Build identification string (arch, version). */
+const char *drift_version(void);
+
+/* --------------------------------------------------------- format layer */
+/* MiniFloat.maxFinite / minSubnormal of a format
+ * (java/.../fmt/MiniFloat.java:61-68, :106). Pure host arithmetic. */
+int drift_format_info(int fmt, double *max_finite, double *min_normal,
+                      double *min_subnormal, int32_t *width);
+
+/* MiniFloat.encode(v, rm, rng) over an array, element order
+ * (java/.../fmt/MiniFloat.java:156-211). codes[i] is the bit pattern. */
+int drift_encode(drift_ctx *ctx, int fmt, int rounding, const double *v,
+                 int32_t *codes, int64_t n, uint64_t *rng_state);
+
+/* MiniFloat.decode(bits) over an array (java/.../fmt/MiniFloat.java:117-142).
+ * A code wider than the format is DRIFT_EINVAL, as Java throws. */
+int drift_decode(drift_ctx *ctx, int fmt, const int32_t *codes, double *v,
+                 int64_t n);
+
+/* Dot.round(x, acc, rm, rng) over an array, element order
+ * (java/.../kernel/Dot.java:141-182). acc is DRIFT_ACC_FP16 or _BF16. */
+int drift_acc_round(drift_ctx *ctx, int acc, int rounding, const double *x,
+                    double *y, int64_t n, uint64_t *rng_state);
+
+/* ---------------------------------------------------------- quant layer */
+/* Quant.amax (java/.../kernel/Quant.java:25-34). NaN is ignored. */
+int drift_amax(drift_ctx *ctx, const double *x, int64_t n, double *amax_out);
+
+/* Quant.perTensorScale (java/.../kernel/Quant.java:37-42). Host arithmetic. */
+int drift_per_tensor_scale(int fmt, double amax, double *scale_out);
+
+/*
+ * Quant.quantize(src, 0, dst, 0, n, f, p, rm, scale, rng)
+ * (java/.../kernel/Quant.java:56-82, MX at :95-123). fmt DRIFT_FMT_NONE copies.
+ * clamped_out (may be NULL) receives the Java return value, widened to int64.
+ * rng_state may be NULL when no draw is needed; a needed draw with a NULL
+ * rng_state is DRIFT_EINVAL (Java: IllegalArgumentException).
+ */
+int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt,
+                   int rounding, const double *src, double *dst, int64_t n,
+                   double scale, uint64_t *rng_state, int64_t *clamped_out);
+
+/* ------------------------------------------------------------ dot layer */
+/*
+ * C[i*c_row_stride + o] = Dot.dot(A, a_off + i*a_row_stride, a_k_stride,
+ *                                 B, b_off + o*b_row_stride, b_k_stride,
+ *                                 K, p, rng) (+ bias[o] when bias != NULL)
+ * for i in [0,M), o in [0,N): the double loops of
+ * java/.../train/Pass.java:200-204 (forward), :222-226 (dgrad, B strided),
+ * :228-232 (wgrad, both strided), java/.../tools/DotSweep.java:121 (M=N=1)
+ * and java/.../tools/RealDotSweep.java:247-254. Dot.dot itself is
+ * java/.../kernel/Dot.java:26-121. Strides may be any non-negative values.
+ * The accumulator rounding may not be STOCHASTIC (DRIFT_EUNSUPPORTED): its
+ * random stream is consumed in output order across dots.
+ */
+int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N,
+               int64_t K, const double *A, int64_t a_off, int64_t a_row_stride,
+               int64_t a_k_stride, const double *B, int64_t b_off,
+               int64_t b_row_stride, int64_t b_k_stride, const double *bias,
+               double *C, int64_t c_row_stride, uint64_t *rng_state);
+
+/* ------------------------------------------ device-resident entry points */
+/* As drift_amax; amax lands in the device double *d_amax. */
+int drift_amax_dev(drift_ctx *ctx, const double *d_x, int64_t n,
+                   double *d_amax, void *stream);
+
+/*
+ * As drift_quantize on device buffers. The per-tensor scale is read from the
+ * device double *d_scale when non-NULL, else `scale` is used. Clamp counts are
+ * ADDED to the device int64 *d_clamped (may be NULL). For stochastic rounding
+ * the Rng state lives in the device uint64 *d_rng_state, which the call
+ * advances on the device (no host round trip). Errors raised on the device
+ * (NaN into a finite format, a needed draw with d_rng_state NULL) are reported
+ * by drift_check_dev.
+ */
+int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt,
+                       int rounding, const double *d_src, double *d_dst,
+                       int64_t n, const double *d_scale, double scale,
+                       uint64_t *d_rng_state, int64_t *d_clamped,
+                       void *stream);
+
+/* As drift_gemm on device buffers (offsets folded into the pointers). */
+int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
+                   int64_t N, int64_t K, const double *d_A,
+                   int64_t a_row_stride, int64_t a_k_stride, const double *d_B,
+                   int64_t b_row_stride, int64_t b_k_stride,
+                   const double *d_bias, double *d_C, int64_t c_row_stride,
+                   void *stream);
+
+/*
+ * Synchronises `stream` and returns the first device-side error raised since
+ * the last check on this context (DRIFT_ENAN_FINITE, DRIFT_EINVAL,
+ * DRIFT_ETIMEOUT), clearing it.
+ */
+int drift_check_dev(drift_ctx *ctx, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRIFT_B200_H */
