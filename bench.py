@@ -1,0 +1,454 @@
+#!/usr/bin/env python
+"""bench.py — emulated MAC/s of the policy sweep on B200.
+
+Workload (the reference's large policy sweep): GEMMs of M = N = K = 8192 on
+N(0,1) x lognormal(0,1) inputs held as fp32 values in doubles; the 12
+accumulator x order x cast policies of RealDotSweep
+(java/src/main/java/io/drift/tools/RealDotSweep.java:212-223) plus the FP64
+exact GEMM they are scored against. One step on one rank is one seed: cast,
+contract and score all 12 policies and run the exact GEMM. Each rank takes its
+own seed (rank + world * step), so per-GPU work is fixed as GPUs are added
+(weak scaling); at 8 GPUs one step is the whole 12 x 8 sweep. Error and clamp
+statistics are summed across ranks with NCCL all-reduce.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--size 8192]
+    python bench.py --impl reference ...   # the oracle, timed on the host cores
+
+`value` counts every emulated multiply-accumulate (13 GEMMs per step per
+rank) over the max-over-ranks device time of the K timed steps. `e2e` runs the
+same steps through the C ABI with pinned host buffers (every input copied in
+and every output copied out inside the timed region).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "bit-exact emulated MAC/s per policy at 1/2/4/8 B200 vs Java host; mismatches=0"
+UNIT = "emulated MAC/s"
+
+
+def sweep_policies(d):
+    """RealDotSweep's policy list (RealDotSweep.java:212-223): the 9
+    accumulator x order policies, the bf16 cast, e4m3 per-tensor and e4m3 MX32."""
+    F, A, O, S = d.Formats, d.Acc, d.Order, d.Scaling
+    b = d.NumericPolicy.builder
+    ps = []
+    for acc in (A.FP32, A.FP16, A.BF16):
+        for o in (O.SEQUENTIAL, O.PAIRWISE, O.BLOCKED):
+            name = f"{acc.name.lower()} {o.name.lower()}"
+            ps.append(b(name).acc(acc).order(o).acc_block(32).build())
+    ps.append(b("bf16 cast").input(F.BF16).build())
+    ps.append(b("e4m3 per-tensor cast").input(F.E4M3).scaling(S.PER_TENSOR).build())
+    ps.append(b("e4m3 mx32 cast").input(F.E4M3).scaling(S.MX_BLOCK).build())
+    return ps
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while a region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.device),
+                                      f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=5).stdout
+                for line in out.strip().splitlines():
+                    self.rows.append([c.strip() for c in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=6)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in self.rows for k in range(4)
+                          if len(r) > 5 + k and r[5 + k].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------ distributed
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ------------------------------------------------------------------ CPU baseline
+
+def cpu_baseline(size: int, budget_s: float, threads: int | None = None):
+    """Times the oracle (the C restatement of the Java path) on this host's
+    cores over a bounded sample of the same sweep: for each of the 13 GEMMs,
+    R rows of A against C rows of B with the full K = size terms (R x C
+    outputs). Per-tensor scales come from the full tensors, as in the real
+    job; the casts themselves run before the clock starts (over the whole job
+    they are about 1e-4 of the contraction work). Returns (MAC/s, threads,
+    description)."""
+    import numpy as np
+    from oracle import oracle as O
+
+    threads = threads or os.cpu_count() or 1
+    rs = np.random.default_rng(0)
+    K = size
+    cols = min(size, 512)
+    full_a = (rs.standard_normal(size * K, dtype=np.float32) *
+              np.exp(rs.standard_normal(size * K, dtype=np.float32))).astype(np.float64)
+    full_b = (rs.standard_normal(size * K, dtype=np.float32) *
+              np.exp(rs.standard_normal(size * K, dtype=np.float32))).astype(np.float64)
+    amax_a, amax_b = O.amax(full_a), O.amax(full_b)
+    pols = [O.policy(acc=O.ACC_FP64)]
+    for acc in (O.ACC_FP32, O.ACC_FP16, O.ACC_BF16):
+        for order in (O.SEQUENTIAL, O.PAIRWISE, O.BLOCKED):
+            pols.append(O.policy(acc=acc, order=order))
+    pols.append(O.policy(input_format=O.BF16))
+    pols.append(O.policy(input_format=O.E4M3, scaling=O.PER_TENSOR))
+    pols.append(O.policy(input_format=O.E4M3, scaling=O.MX_BLOCK))
+    B = full_b[:cols * K].copy()
+    # Calibrate the row count so the timed sample takes about budget_s.
+    A1 = full_a[:K * threads].copy()
+    t0 = time.perf_counter()
+    O.gemm(pols[4], threads, min(cols, 64), K, A1, 0, K, 1, B, 0, K, 1, threads=threads)
+    per_mac = (time.perf_counter() - t0) / (threads * min(cols, 64) * K)
+    rows = int(budget_s / len(pols) / (per_mac * cols * K * 1.5)) // threads * threads
+    rows = max(threads, min(rows, size))
+    A = full_a[:rows * K].copy()
+    operands = []
+    for p in pols:
+        if p.input_format < 0:
+            operands.append((A, B))
+            continue
+        f = p.input_format
+        sa = O.per_tensor_scale(f, amax_a) if p.scaling == O.PER_TENSOR else 1.0
+        sb = O.per_tensor_scale(f, amax_b) if p.scaling == O.PER_TENSOR else 1.0
+        operands.append((O.quantize(p, f, 0, A, sa)[0], O.quantize(p, f, 0, B, sb)[0]))
+    macs = 0
+    t0 = time.perf_counter()
+    for p, (qa, qb) in zip(pols, operands):
+        O.gemm(p, rows, cols, K, qa, 0, K, 1, qb, 0, K, 1, threads=threads)
+        macs += rows * cols * K
+    dt = time.perf_counter() - t0
+    desc = (f"oracle (C restatement of the Java path, -O2, no FMA) on {threads} host threads: "
+            f"{len(pols)} GEMMs of {rows} x {cols} outputs with K={K}; {macs:.3e} MACs in "
+            f"{dt:.1f} s")
+    return macs / dt, threads, desc
+
+
+# ------------------------------------------------------------------ engine arm
+
+def run_engine(args):
+    import numpy as np
+    import torch
+    import drift_b200 as d
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    d.Context.use_device(local)
+    ctx = d.Context.current()
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    stream = torch.cuda.current_stream()
+    S = args.size
+    M = N = K = S
+    pols = sweep_policies(d)
+    exact_p = d.NumericPolicy.exact()
+    dev = torch.device("cuda", local)
+
+    def make_inputs(seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + seed)
+        x = torch.randn(S, S, device=dev, generator=g, dtype=torch.float32)
+        x *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float32))
+        y = torch.randn(S, S, device=dev, generator=g, dtype=torch.float32)
+        y *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float32))
+        return x.double(), y.double()
+
+    A, B = make_inputs(rank)
+    qA = torch.empty_like(A)
+    qB = torch.empty_like(B)
+    C = torch.empty((M, N), dtype=torch.float64, device=dev)
+    Cx = torch.empty((M, N), dtype=torch.float64, device=dev)
+    n_pol = len(pols)
+    sums = torch.zeros((n_pol, 2), dtype=torch.float64, device=dev)
+    clamps = torch.zeros((n_pol,), dtype=torch.int64, device=dev)
+    scal = torch.zeros((4,), dtype=torch.float64, device=dev)  # amax A, amax B, scale A, scale B
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n_pol + 1)]
+    gemm_ms = [0.0] * (n_pol + 1)
+    launches = [0]
+
+    def cast(p, src, dst, slot, clamp_slot):
+        f = p.input_format
+        if f is None:
+            return src
+        if p.scaling == d.Scaling.PER_TENSOR:
+            d.amax_dev(src, scal[slot:slot + 1], ctx=ctx)
+            d.per_tensor_scale_dev(f, scal[slot:slot + 1], scal[2 + slot:3 + slot], ctx=ctx)
+            d.quantize_dev(p, f, p.input_rounding, src, dst, d_scale=scal[2 + slot:3 + slot],
+                           d_clamped=clamps[clamp_slot:clamp_slot + 1], ctx=ctx)
+            launches[0] += 3
+        else:
+            d.quantize_dev(p, f, p.input_rounding, src, dst,
+                           d_clamped=clamps[clamp_slot:clamp_slot + 1], ctx=ctx)
+            launches[0] += 1
+        return dst
+
+    def step(timed_gemms: bool):
+        ev[0][0].record(stream)
+        d.gemm_dev(exact_p, A, B, Cx, ctx=ctx)
+        ev[0][1].record(stream)
+        launches[0] += 1
+        for k, p in enumerate(pols):
+            a = cast(p, A, qA, 0, k)
+            b = cast(p, B, qB, 1, k)
+            ev[k + 1][0].record(stream)
+            d.gemm_dev(p, a, b, C, ctx=ctx)
+            ev[k + 1][1].record(stream)
+            d.error_sums_dev(C, Cx, sums[k], ctx=ctx)
+            launches[0] += 2
+        if pg is not None:
+            pg.all_reduce(sums)
+            pg.all_reduce(clamps)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if pg is not None:
+            pg.barrier()
+            torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(False)
+    d.check_dev(ctx=ctx)
+    barrier()
+    sums.zero_()
+    clamps.zero_()
+    launches[0] = 0
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        t_start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        t_end.record(stream)
+        barrier()
+    # Per-GEMM device times of the last step (events on the launching stream).
+    for k in range(n_pol + 1):
+        gemm_ms[k] = ev[k][0].elapsed_time(ev[k][1])
+    d.check_dev(ctx=ctx)
+    ms = t_start.elapsed_time(t_end)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms_max = float(t.item())
+    macs_per_step_rank = (n_pol + 1) * M * N * K
+    value = macs_per_step_rank * world * args.steps / (ms_max * 1e-3)
+
+    # Roofline of the dominant kernel (the contraction): FP64-pipe work is 2
+    # operations (DMUL + DADD) per emulated MAC; the peak is this GPU's
+    # measured DMUL+DADD rate.
+    fp64_peak = d.probe_fp64(ctx)
+    gemm_total_ms = sum(gemm_ms)
+    achieved = 2.0 * macs_per_step_rank / (gemm_total_ms * 1e-3)
+    per_policy = {"exact fp64": M * N * K / (gemm_ms[0] * 1e-3)}
+    for k, p in enumerate(pols):
+        per_policy[p.name] = M * N * K / (gemm_ms[k + 1] * 1e-3)
+
+    # Statistics (summed over ranks): RMS ratio and clamps per pair.
+    s = sums.cpu().numpy()
+    c = clamps.cpu().numpy()
+    stats = {p.name: {"rms_error_ratio": float(np.sqrt(s[k, 0] / s[k, 1])),
+                      "clamped_per_pair": float(c[k]) / (args.steps * world * M * N)}
+             for k, p in enumerate(pols)}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(d, args, A, B, pols, exact_p, world, rank, pg)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        v, cores, desc = cpu_baseline(S, args.cpu_budget)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}
+
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic: N(0,1) x lognormal(0,1) fp32 values held in doubles, seeded per rank",
+        "config": {"workload": f"policy sweep GEMM M=N=K={S}, 12 policies + exact FP64, "
+                               f"1 seed per rank per step", "M": M, "N": N, "K": K,
+                   "policies": [p.name for p in pols], "seeds_per_step": world,
+                   "l2": "inputs (2 x 512 MiB at 8192) are larger than L2",
+                   "parallelism": f"shard by seed x{world}"},
+        "roofline": {"bound": "fp64", "achieved": achieved / 1e12, "peak": fp64_peak / 1e12,
+                     "unit": "TFLOP/s", "frac": achieved / fp64_peak, "traffic": None,
+                     "kernel": "gemm_kernel (all policies)",
+                     "peak_source": "measured DMUL+DADD probe (drift_probe_fp64) on this GPU"},
+        "per_policy_mac_per_s": per_policy,
+        "stats": stats,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+        "gpu_launches": launches[0],
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_e2e(d, args, A, B, pols, exact_p, world, rank, pg):
+    """The same steps through the reference-facing host entry points
+    (drift_quantize / drift_gemm on pinned host buffers)."""
+    import numpy as np
+    import torch
+
+    S = args.size
+    hA = torch.empty((S, S), dtype=torch.float64, pin_memory=True)
+    hB = torch.empty((S, S), dtype=torch.float64, pin_memory=True)
+    hA.copy_(A)
+    hB.copy_(B)
+    hqA = torch.empty_like(hA, pin_memory=True)
+    hqB = torch.empty_like(hB, pin_memory=True)
+    hC = torch.empty_like(hA, pin_memory=True)
+    a, b, qa, qb, cc = (x.numpy() for x in (hA, hB, hqA, hqB, hC))
+    h2d = d2h = 0
+
+    def one_step():
+        nonlocal h2d, d2h
+        h2d = d2h = 0
+        d.gemm(exact_p, S, S, S, a, 0, S, 1, b, 0, S, 1, out=cc)
+        h2d += 2 * a.nbytes
+        d2h += cc.nbytes
+        for p in pols:
+            x, y = a, b
+            f = p.input_format
+            if f is not None:
+                sa = d.Quant.per_tensor_scale(f, d.Quant.amax(a)) if p.scaling == 1 else 1.0
+                sb = d.Quant.per_tensor_scale(f, d.Quant.amax(b)) if p.scaling == 1 else 1.0
+                d.Quant.quantize(a, 0, qa, 0, a.size, f, p, sa, None)
+                d.Quant.quantize(b, 0, qb, 0, b.size, f, p, sb, None)
+                h2d += 2 * a.nbytes + (2 * a.nbytes if p.scaling == 1 else 0)
+                d2h += 2 * a.nbytes
+                x, y = qa, qb
+            d.gemm(p, S, S, S, x, 0, S, 1, y, 0, S, 1, out=cc)
+            h2d += 2 * a.nbytes
+            d2h += cc.nbytes
+
+    one_step()  # warm-up
+    steps = max(1, args.e2e_steps)
+    if pg is not None:
+        pg.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_step()
+    dt = time.perf_counter() - t0
+    tt = torch.tensor([dt], dtype=torch.float64, device="cuda")
+    if pg is not None:
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+    dt = float(tt.item())
+    macs = (len(pols) + 1) * S ** 3 * world * steps
+    return {"value": macs / dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "path": "drift_quantize/drift_amax/drift_gemm on pinned host buffers"}
+
+
+# ------------------------------------------------------------------ reference arm
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return 0
+    vals = []
+    desc = cores = None
+    for _ in range(args.warmup):
+        cpu_baseline(args.size, min(5.0, args.cpu_budget / 4))
+    for _ in range(args.steps):
+        v, cores, desc = cpu_baseline(args.size, args.cpu_budget / max(1, args.steps))
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "impl": "reference",
+        "data": "synthetic: N(0,1) x lognormal(0,1) fp32 values held in doubles",
+        "config": {"workload": f"policy sweep GEMM M=N=K={args.size}, 12 policies + exact FP64, "
+                               "row sample", "M": args.size, "N": args.size, "K": args.size},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "no JVM on this image: the reference's Java path is timed through its C "
+                "restatement (the oracle), with all host threads",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--size", type=int, default=8192)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "engine":
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_engine(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,21 @@
+"""drift_b200 — a B200-native engine for drift's policy-parameterised emulated matmul.
+
+The Python surface mirrors the reference's Java API (io.drift.fmt and
+io.drift.kernel): Formats / MiniFloat / Rounding / Rng, NumericPolicy, Quant,
+Dot, and the named Policies. Every cast and every contraction runs in the
+CUDA engine (libdrift_b200.so, sm_100a) through its C ABI
+(include/drift_b200.h); importing the package loads it and fails if it cannot.
+"""
+from . import _lib
+from ._lib import Context, DriftError
+from .fmt import Formats, MiniFloat, Rng, Rounding, Specials
+from .kernel import (Acc, Dot, NumericPolicy, Order, Quant, Scaling, amax_dev, check_dev,
+                     error_sums_dev, gemm, per_tensor_scale_dev, probe_fp64,
+                     gemm_dev, quantize_dev)
+from . import policies
+
+_lib.load()
+
+__all__ = ["Context", "DriftError", "Formats", "MiniFloat", "Rng", "Rounding", "Specials", "Acc",
+           "Dot", "NumericPolicy", "Order", "Quant", "Scaling", "gemm", "gemm_dev", "quantize_dev",
+           "amax_dev", "check_dev", "policies"]

@@ -1,0 +1,472 @@
+// capi.cu — the C ABI (include/drift_b200.h): contexts, host-buffer entry
+// points that stage through device memory, and device-resident entry points.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace drift;
+
+// ------------------------------------------------------------------ errors
+
+static thread_local std::string g_last_error;
+
+static int fail(int status, const char *what) {
+    g_last_error = what;
+    return status;
+}
+
+static int cuda_fail(cudaError_t e, const char *what) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return DRIFT_ECUDA;
+}
+
+#define CUDA_TRY(call, what)                       \
+    do {                                           \
+        cudaError_t e_ = (call);                   \
+        if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+    } while (0)
+
+// ------------------------------------------------------------------ formats
+
+namespace drift {
+
+// Formats.java:20-45 through the MiniFloat constructor (MiniFloat.java:70-107).
+bool fmt_desc(int id, FmtDesc *out) {
+    static const int table[DRIFT_NUM_FORMATS][4] = {
+        {4, 3, 7, SP_FN},       {5, 2, 15, SP_IEEE}, {2, 1, 1, SP_FINITE},
+        {3, 2, 3, SP_FINITE},   {2, 3, 1, SP_FINITE}, {5, 10, 15, SP_IEEE},
+        {8, 7, 127, SP_IEEE},
+    };
+    if (id < 0 || id >= DRIFT_NUM_FORMATS) return false;
+    const int e = table[id][0], m = table[id][1], bias = table[id][2], sp = table[id][3];
+    FmtDesc f;
+    f.mant_bits = m;
+    f.bias = bias;
+    f.specials = sp;
+    f.max_exp_field = (1 << e) - 1;
+    f.mant_mask = (1 << m) - 1;
+    f.exp_mask = f.max_exp_field << m;
+    f.sign_bit = 1 << (e + m);
+    f.code_mask = (1 << (1 + e + m)) - 1;
+    f.min_normal_exp = 1 - bias;
+    int top_exp, top_mant;
+    if (sp == SP_IEEE) {
+        top_exp = f.max_exp_field - 1;
+        top_mant = f.mant_mask;
+        f.nan_bits = f.exp_mask | 1;
+    } else if (sp == SP_FN) {
+        top_exp = f.max_exp_field;
+        top_mant = f.mant_mask - 1;
+        f.nan_bits = f.exp_mask | f.mant_mask;
+    } else {
+        top_exp = f.max_exp_field;
+        top_mant = f.mant_mask;
+        f.nan_bits = 0;
+    }
+    f.max_finite_bits = (top_exp << m) | top_mant;
+    f.max_finite = std::ldexp(1.0 + (double)top_mant / (1 << m), top_exp - bias);
+    f.emax = java_get_exponent(f.max_finite);
+    *out = f;
+    return true;
+}
+
+void *Workspace::get(size_t bytes, cudaStream_t st) {
+    if (bytes <= cap_ && ptr_) return ptr_;
+    if (ptr_) cudaFreeAsync(ptr_, st);
+    ptr_ = nullptr;
+    cap_ = 0;
+    size_t want = bytes < 4096 ? 4096 : bytes;
+    if (cudaMallocAsync(&ptr_, want, st) != cudaSuccess) {
+        ptr_ = nullptr;
+        return nullptr;
+    }
+    cap_ = want;
+    return ptr_;
+}
+
+void Workspace::release(cudaStream_t st) {
+    if (ptr_) cudaFreeAsync(ptr_, st);
+    ptr_ = nullptr;
+    cap_ = 0;
+}
+
+const uint8_t *ScheduleCache::get(int64_t K, cudaStream_t st) {
+    (void)st;
+    auto it = entries_.find(K);
+    if (it != entries_.end()) return it->second.d;
+    std::vector<uint8_t> sched;
+    int depth = 0;
+    status_ = pairwise_schedule(K, sched, &depth);
+    if (status_ != DRIFT_OK) return nullptr;
+    uint8_t *d = nullptr;
+    if (cudaMalloc(&d, sched.size()) != cudaSuccess) {
+        status_ = DRIFT_ENOMEM;
+        return nullptr;
+    }
+    if (cudaMemcpy(d, sched.data(), sched.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaFree(d);
+        status_ = DRIFT_ECUDA;
+        return nullptr;
+    }
+    const int64_t leaves = (int64_t)(sched.size() - 1) / 2;
+    entries_[K] = Entry{d, leaves};
+    return d;
+}
+
+int64_t ScheduleCache::leaves(int64_t K) const {
+    auto it = entries_.find(K);
+    return it == entries_.end() ? 0 : it->second.leaves;
+}
+
+void ScheduleCache::clear() {
+    for (auto &kv : entries_) cudaFree(kv.second.d);
+    entries_.clear();
+}
+
+}  // namespace drift
+
+// ------------------------------------------------------------------ context
+
+struct drift_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    Workspace ws;       // kernel scratch
+    Workspace io;       // staging for host-buffer calls
+    ScheduleCache sched;
+    // Small device words: [0] error flags (int), [8] rng state, [16] clamp
+    // counter, [24] scalar result.
+    char *d_small = nullptr;
+    int *d_err() { return (int *)d_small; }
+    uint64_t *d_state() { return (uint64_t *)(d_small + 8); }
+    unsigned long long *d_clamped() { return (unsigned long long *)(d_small + 16); }
+    double *d_scalar() { return (double *)(d_small + 24); }
+};
+
+static int enter(drift_ctx *ctx) {
+    if (!ctx) return fail(DRIFT_EINVAL, "null context");
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    return DRIFT_OK;
+}
+
+static cudaStream_t pick(drift_ctx *ctx, void *stream) {
+    return stream ? (cudaStream_t)stream : ctx->stream;
+}
+
+// Reads and clears the device error word; maps it to a status.
+static int take_device_error(drift_ctx *ctx, cudaStream_t st) {
+    int flags = 0;
+    CUDA_TRY(cudaMemcpyAsync(&flags, ctx->d_err(), sizeof(int), cudaMemcpyDeviceToHost, st),
+             "read error word");
+    CUDA_TRY(cudaMemsetAsync(ctx->d_err(), 0, sizeof(int), st), "clear error word");
+    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    if (flags & DEV_ERR_NAN_FINITE) return fail(DRIFT_ENAN_FINITE, "NaN cast into a format without NaN");
+    if (flags & DEV_ERR_NO_RNG) return fail(DRIFT_EINVAL, "stochastic rounding needs an Rng");
+    if (flags & DEV_ERR_TIMEOUT) return fail(DRIFT_ETIMEOUT, "device wait gave up");
+    return DRIFT_OK;
+}
+
+extern "C" {
+
+const char *drift_last_error(void) { return g_last_error.c_str(); }
+
+const char *drift_version(void) { return "drift_b200 0.1 (sm_100a)"; }
+
+int drift_open(int device, drift_ctx **out) {
+    if (!out) return fail(DRIFT_EINVAL, "null out");
+    *out = nullptr;
+    int count = 0;
+    CUDA_TRY(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (device < 0 || device >= count) return fail(DRIFT_EINVAL, "no such device");
+    CUDA_TRY(cudaSetDevice(device), "cudaSetDevice");
+    drift_ctx *ctx = new drift_ctx();
+    ctx->device = device;
+    cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_small, 64);
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_small, 0, 64);
+    if (e != cudaSuccess) {
+        if (ctx->stream) cudaStreamDestroy(ctx->stream);
+        delete ctx;
+        return cuda_fail(e, "drift_open");
+    }
+    *out = ctx;
+    return DRIFT_OK;
+}
+
+int drift_close(drift_ctx *ctx) {
+    if (!ctx) return DRIFT_OK;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    ctx->ws.release(ctx->stream);
+    ctx->io.release(ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
+    ctx->sched.clear();
+    cudaFree(ctx->d_small);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return DRIFT_OK;
+}
+
+int drift_format_info(int fmt, double *max_finite, double *min_normal, double *min_subnormal,
+                      int32_t *width) {
+    FmtDesc f;
+    if (!fmt_desc(fmt, &f)) return fail(DRIFT_EINVAL, "bad format id");
+    if (max_finite) *max_finite = f.max_finite;
+    if (min_normal) *min_normal = std::ldexp(1.0, f.min_normal_exp);
+    if (min_subnormal) *min_subnormal = std::ldexp(1.0, f.min_normal_exp - f.mant_bits);
+    if (width) *width = __builtin_popcount((unsigned)f.code_mask);
+    return DRIFT_OK;
+}
+
+int drift_per_tensor_scale(int fmt, double amax, double *scale_out) {
+    FmtDesc f;
+    if (!fmt_desc(fmt, &f) || !scale_out) return fail(DRIFT_EINVAL, "bad format id");
+    *scale_out = (amax == 0.0 || !std::isfinite(amax)) ? 1.0 : f.max_finite / amax;
+    return DRIFT_OK;
+}
+
+// ------------------------------------------------------------------ host-buffer calls
+
+int drift_encode(drift_ctx *ctx, int fmt, int rounding, const double *v, int32_t *codes,
+                 int64_t n, uint64_t *rng_state) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || (n > 0 && (!v || !codes))) return fail(DRIFT_EINVAL, "bad arguments");
+    if (n == 0) return DRIFT_OK;
+    cudaStream_t st = ctx->stream;
+    char *buf = (char *)ctx->io.get((size_t)n * 12 + 256, st);
+    if (!buf) return fail(DRIFT_ENOMEM, "staging");
+    double *d_v = (double *)buf;
+    int32_t *d_c = (int32_t *)(buf + n * 8);
+    CUDA_TRY(cudaMemcpyAsync(d_v, v, n * 8, cudaMemcpyHostToDevice, st), "copy in");
+    if (rng_state)
+        CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), rng_state, 8, cudaMemcpyHostToDevice, st), "rng in");
+    rc = launch_encode(ctx->ws, fmt, rounding, d_v, d_c, n, rng_state ? ctx->d_state() : nullptr,
+                       ctx->d_err(), st);
+    if (rc) return fail(rc, "encode launch");
+    uint64_t state = 0;
+    CUDA_TRY(cudaMemcpyAsync(codes, d_c, n * 4, cudaMemcpyDeviceToHost, st), "copy out");
+    if (rng_state)
+        CUDA_TRY(cudaMemcpyAsync(&state, ctx->d_state(), 8, cudaMemcpyDeviceToHost, st), "rng out");
+    rc = take_device_error(ctx, st);
+    if (rc) return rc;
+    if (rng_state) *rng_state = state;
+    return DRIFT_OK;
+}
+
+int drift_decode(drift_ctx *ctx, int fmt, const int32_t *codes, double *v, int64_t n) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    FmtDesc f;
+    if (!fmt_desc(fmt, &f)) return fail(DRIFT_EINVAL, "bad format id");
+    if (n < 0 || (n > 0 && (!v || !codes))) return fail(DRIFT_EINVAL, "bad arguments");
+    for (int64_t i = 0; i < n; i++)  // MiniFloat.java:118-120
+        if (codes[i] & ~f.code_mask) return fail(DRIFT_EINVAL, "bits outside format width");
+    if (n == 0) return DRIFT_OK;
+    cudaStream_t st = ctx->stream;
+    char *buf = (char *)ctx->io.get((size_t)n * 12 + 256, st);
+    if (!buf) return fail(DRIFT_ENOMEM, "staging");
+    double *d_v = (double *)buf;
+    int32_t *d_c = (int32_t *)(buf + n * 8);
+    CUDA_TRY(cudaMemcpyAsync(d_c, codes, n * 4, cudaMemcpyHostToDevice, st), "copy in");
+    rc = launch_decode(fmt, d_c, d_v, n, st);
+    if (rc) return fail(rc, "decode launch");
+    CUDA_TRY(cudaMemcpyAsync(v, d_v, n * 8, cudaMemcpyDeviceToHost, st), "copy out");
+    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    return DRIFT_OK;
+}
+
+int drift_acc_round(drift_ctx *ctx, int acc, int rounding, const double *x, double *y, int64_t n,
+                    uint64_t *rng_state) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || (n > 0 && (!x || !y))) return fail(DRIFT_EINVAL, "bad arguments");
+    if (n == 0) return DRIFT_OK;
+    cudaStream_t st = ctx->stream;
+    char *buf = (char *)ctx->io.get((size_t)n * 16 + 256, st);
+    if (!buf) return fail(DRIFT_ENOMEM, "staging");
+    double *d_x = (double *)buf;
+    double *d_y = (double *)(buf + n * 8);
+    CUDA_TRY(cudaMemcpyAsync(d_x, x, n * 8, cudaMemcpyHostToDevice, st), "copy in");
+    if (rng_state)
+        CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), rng_state, 8, cudaMemcpyHostToDevice, st), "rng in");
+    rc = launch_acc_round(ctx->ws, acc, rounding, d_x, d_y, n,
+                          rng_state ? ctx->d_state() : nullptr, ctx->d_err(), st);
+    if (rc) return fail(rc, "acc_round launch");
+    uint64_t state = 0;
+    CUDA_TRY(cudaMemcpyAsync(y, d_y, n * 8, cudaMemcpyDeviceToHost, st), "copy out");
+    if (rng_state)
+        CUDA_TRY(cudaMemcpyAsync(&state, ctx->d_state(), 8, cudaMemcpyDeviceToHost, st), "rng out");
+    rc = take_device_error(ctx, st);
+    if (rc) return rc;
+    if (rng_state) *rng_state = state;
+    return DRIFT_OK;
+}
+
+int drift_amax(drift_ctx *ctx, const double *x, int64_t n, double *amax_out) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || !amax_out || (n > 0 && !x)) return fail(DRIFT_EINVAL, "bad arguments");
+    cudaStream_t st = ctx->stream;
+    double *d_x = nullptr;
+    if (n > 0) {
+        d_x = (double *)ctx->io.get((size_t)n * 8, st);
+        if (!d_x) return fail(DRIFT_ENOMEM, "staging");
+        CUDA_TRY(cudaMemcpyAsync(d_x, x, n * 8, cudaMemcpyHostToDevice, st), "copy in");
+    }
+    rc = launch_amax(d_x, n, ctx->d_scalar(), st);
+    if (rc) return fail(rc, "amax launch");
+    CUDA_TRY(cudaMemcpyAsync(amax_out, ctx->d_scalar(), 8, cudaMemcpyDeviceToHost, st), "copy out");
+    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    return DRIFT_OK;
+}
+
+int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt, int rounding, const double *src,
+                   double *dst, int64_t n, double scale, uint64_t *rng_state,
+                   int64_t *clamped_out) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || n < 0 || (n > 0 && (!src || !dst))) return fail(DRIFT_EINVAL, "bad arguments");
+    if (clamped_out) *clamped_out = 0;
+    if (n == 0) return DRIFT_OK;
+    cudaStream_t st = ctx->stream;
+    char *buf = (char *)ctx->io.get((size_t)n * 16 + 256, st);
+    if (!buf) return fail(DRIFT_ENOMEM, "staging");
+    double *d_src = (double *)buf;
+    double *d_dst = (double *)(buf + n * 8);
+    CUDA_TRY(cudaMemcpyAsync(d_src, src, n * 8, cudaMemcpyHostToDevice, st), "copy in");
+    CUDA_TRY(cudaMemsetAsync(ctx->d_clamped(), 0, 8, st), "clear clamps");
+    if (rng_state)
+        CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), rng_state, 8, cudaMemcpyHostToDevice, st), "rng in");
+    rc = launch_quantize(ctx->ws, p, fmt, rounding, d_src, d_dst, n, nullptr, scale,
+                         rng_state ? ctx->d_state() : nullptr, ctx->d_clamped(), ctx->d_err(), st);
+    if (rc) return fail(rc, "quantize launch");
+    uint64_t state = 0;
+    unsigned long long clamped = 0;
+    CUDA_TRY(cudaMemcpyAsync(dst, d_dst, n * 8, cudaMemcpyDeviceToHost, st), "copy out");
+    CUDA_TRY(cudaMemcpyAsync(&clamped, ctx->d_clamped(), 8, cudaMemcpyDeviceToHost, st), "clamps out");
+    if (rng_state)
+        CUDA_TRY(cudaMemcpyAsync(&state, ctx->d_state(), 8, cudaMemcpyDeviceToHost, st), "rng out");
+    rc = take_device_error(ctx, st);
+    if (rc) return rc;
+    if (rng_state) *rng_state = state;
+    if (clamped_out) *clamped_out = (int64_t)clamped;
+    return DRIFT_OK;
+}
+
+// Number of elements an operand with these strides spans from its offset.
+static int64_t span_of(int64_t rows, int64_t rs, int64_t K, int64_t ks) {
+    if (rows <= 0 || K <= 0) return 0;
+    return (rows - 1) * rs + (K - 1) * ks + 1;
+}
+
+int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int64_t K,
+               const double *A, int64_t a_off, int64_t a_row_stride, int64_t a_k_stride,
+               const double *B, int64_t b_off, int64_t b_row_stride, int64_t b_k_stride,
+               const double *bias, double *C, int64_t c_row_stride, uint64_t *rng_state) {
+    (void)rng_state;  // no accumulator this engine supports draws random numbers
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || M < 0 || N < 0 || K < 0 || a_off < 0 || b_off < 0 || a_row_stride < 0 ||
+        a_k_stride < 0 || b_row_stride < 0 || b_k_stride < 0 || c_row_stride < N)
+        return fail(DRIFT_EINVAL, "bad shape or stride");
+    if (M == 0 || N == 0) return DRIFT_OK;
+    if (!C || (K > 0 && (!A || !B))) return fail(DRIFT_EINVAL, "null buffer");
+    cudaStream_t st = ctx->stream;
+    const int64_t sa = span_of(M, a_row_stride, K, a_k_stride);
+    const int64_t sb = span_of(N, b_row_stride, K, b_k_stride);
+    const int64_t sc = M * N;
+    const int64_t total = sa + sb + sc + (bias ? N : 0) + 8;
+    char *buf = (char *)ctx->io.get((size_t)total * 8 + 512, st);
+    if (!buf) return fail(DRIFT_ENOMEM, "staging");
+    double *d_a = (double *)buf;
+    double *d_b = d_a + ((sa + 1) & ~1LL);
+    double *d_c = d_b + ((sb + 1) & ~1LL);
+    double *d_bias = bias ? d_c + ((sc + 1) & ~1LL) : nullptr;
+    if (sa) CUDA_TRY(cudaMemcpyAsync(d_a, A + a_off, sa * 8, cudaMemcpyHostToDevice, st), "copy A");
+    if (sb) CUDA_TRY(cudaMemcpyAsync(d_b, B + b_off, sb * 8, cudaMemcpyHostToDevice, st), "copy B");
+    if (bias) CUDA_TRY(cudaMemcpyAsync(d_bias, bias, N * 8, cudaMemcpyHostToDevice, st), "copy bias");
+    rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
+                     b_row_stride, b_k_stride, d_bias, d_c, N, st);
+    if (rc) return fail(rc, rc == DRIFT_EUNSUPPORTED ? "stochastic accumulator rounding is not supported"
+                                                     : "gemm launch");
+    CUDA_TRY(cudaMemcpy2DAsync(C, c_row_stride * 8, d_c, N * 8, N * 8, M, cudaMemcpyDeviceToHost, st),
+             "copy C");
+    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    return DRIFT_OK;
+}
+
+// ------------------------------------------------------------------ device-resident calls
+
+int drift_amax_dev(drift_ctx *ctx, const double *d_x, int64_t n, double *d_amax, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || !d_amax || (n > 0 && !d_x)) return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_amax(d_x, n, d_amax, pick(ctx, stream));
+    return rc ? fail(rc, "amax launch") : DRIFT_OK;
+}
+
+int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt, int rounding,
+                       const double *d_src, double *d_dst, int64_t n, const double *d_scale,
+                       double scale, uint64_t *d_rng_state, int64_t *d_clamped, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || n < 0 || (n > 0 && (!d_src || !d_dst))) return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_quantize(ctx->ws, p, fmt, rounding, d_src, d_dst, n, d_scale, scale, d_rng_state,
+                         (unsigned long long *)d_clamped, ctx->d_err(), pick(ctx, stream));
+    return rc ? fail(rc, "quantize launch") : DRIFT_OK;
+}
+
+int drift_per_tensor_scale_dev(drift_ctx *ctx, int fmt, const double *d_amax, double *d_scale,
+                               void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!d_amax || !d_scale) return fail(DRIFT_EINVAL, "null pointer");
+    rc = launch_per_tensor_scale(fmt, d_amax, d_scale, pick(ctx, stream));
+    return rc ? fail(rc, "per-tensor scale") : DRIFT_OK;
+}
+
+int drift_error_sums_dev(drift_ctx *ctx, const double *d_got, const double *d_exact, int64_t n,
+                         double *d_sums, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || !d_sums || (n > 0 && (!d_got || !d_exact))) return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_error_sums(d_got, d_exact, n, d_sums, pick(ctx, stream));
+    return rc ? fail(rc, "error sums") : DRIFT_OK;
+}
+
+int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int64_t K,
+                   const double *d_A, int64_t a_row_stride, int64_t a_k_stride, const double *d_B,
+                   int64_t b_row_stride, int64_t b_k_stride, const double *d_bias, double *d_C,
+                   int64_t c_row_stride, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || c_row_stride < N) return fail(DRIFT_EINVAL, "bad shape or stride");
+    if (M > 0 && N > 0 && (!d_C || (K > 0 && (!d_A || !d_B)))) return fail(DRIFT_EINVAL, "null buffer");
+    rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
+                     b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, pick(ctx, stream));
+    return rc ? fail(rc, rc == DRIFT_EUNSUPPORTED ? "stochastic accumulator rounding is not supported"
+                                                  : "gemm launch")
+              : DRIFT_OK;
+}
+
+int drift_probe_fp64(drift_ctx *ctx, double *ops_per_s) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!ops_per_s) return fail(DRIFT_EINVAL, "null out");
+    rc = launch_fp64_probe(ctx->stream, ops_per_s);
+    return rc ? fail(rc, "fp64 probe") : DRIFT_OK;
+}
+
+int drift_check_dev(drift_ctx *ctx, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    return take_device_error(ctx, pick(ctx, stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,66 @@
+// internal.h — declarations shared by the engine's translation units.
+#pragma once
+
+#include <cstdint>
+#include <map>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/drift_b200.h"
+
+namespace drift {
+
+// A growable device scratch buffer, allocated and freed in stream order.
+// Every call through one context shares it, so calls on different streams
+// of the same context must not overlap.
+class Workspace {
+   public:
+    void *get(size_t bytes, cudaStream_t st);
+    void release(cudaStream_t st);
+
+   private:
+    void *ptr_ = nullptr;
+    size_t cap_ = 0;
+};
+
+// Device copies of Dot.pairwise leaf schedules, one per K, kept for the
+// life of the context.
+class ScheduleCache {
+   public:
+    const uint8_t *get(int64_t K, cudaStream_t st);
+    int64_t leaves(int64_t K) const;
+    int last_status() const { return status_; }
+    void clear();
+
+   private:
+    struct Entry {
+        uint8_t *d;
+        int64_t leaves;
+    };
+    std::map<int64_t, Entry> entries_;
+    int status_ = DRIFT_OK;
+};
+
+int pairwise_schedule(int64_t K, std::vector<uint8_t> &sched, int *depth);
+
+int launch_amax(const double *d_x, int64_t n, double *d_amax, cudaStream_t st);
+int launch_per_tensor_scale(int fmt, const double *d_amax, double *d_scale, cudaStream_t st);
+int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const double *d_src,
+                    double *d_dst, int64_t n, const double *d_scale, double scale,
+                    uint64_t *d_state, unsigned long long *d_clamped, int *d_err,
+                    cudaStream_t st);
+int launch_encode(Workspace &ws, int fmt, int rm, const double *d_v, int32_t *d_codes, int64_t n,
+                  uint64_t *d_state, int *d_err, cudaStream_t st);
+int launch_decode(int fmt, const int32_t *d_codes, double *d_v, int64_t n, cudaStream_t st);
+int launch_acc_round(Workspace &ws, int acc, int rm, const double *d_x, double *d_y, int64_t n,
+                     uint64_t *d_state, int *d_err, cudaStream_t st);
+int launch_error_sums(const double *got, const double *exact, int64_t n, double *sums,
+                      cudaStream_t st);
+int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
+int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
+                int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
+                int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
+                cudaStream_t st);
+
+}  // namespace drift

@@ -31,6 +31,12 @@
 
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#define DRIFT_API __attribute__((visibility("default")))
+#else
+#define DRIFT_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -119,40 +125,40 @@ typedef struct drift_ctx drift_ctx;
 
 /* ------------------------------------------------------------ lifecycle */
 /* Opens a context on CUDA device `device` with its own stream. */
-int drift_open(int device, drift_ctx **out);
-int drift_close(drift_ctx *ctx);
+DRIFT_API int drift_open(int device, drift_ctx **out);
+DRIFT_API int drift_close(drift_ctx *ctx);
 /* Message for the calling thread's most recent non-OK status. */
-const char *drift_last_error(void);
+DRIFT_API const char *drift_last_error(void);
 /* Build identification string (arch, version). */
-const char *drift_version(void);
+DRIFT_API const char *drift_version(void);
 
 /* --------------------------------------------------------- format layer */
 /* MiniFloat.maxFinite / minSubnormal of a format
  * (java/.../fmt/MiniFloat.java:61-68, :106). Pure host arithmetic. */
-int drift_format_info(int fmt, double *max_finite, double *min_normal,
+DRIFT_API int drift_format_info(int fmt, double *max_finite, double *min_normal,
                       double *min_subnormal, int32_t *width);
 
 /* MiniFloat.encode(v, rm, rng) over an array, element order
  * (java/.../fmt/MiniFloat.java:156-211). codes[i] is the bit pattern. */
-int drift_encode(drift_ctx *ctx, int fmt, int rounding, const double *v,
+DRIFT_API int drift_encode(drift_ctx *ctx, int fmt, int rounding, const double *v,
                  int32_t *codes, int64_t n, uint64_t *rng_state);
 
 /* MiniFloat.decode(bits) over an array (java/.../fmt/MiniFloat.java:117-142).
  * A code wider than the format is DRIFT_EINVAL, as Java throws. */
-int drift_decode(drift_ctx *ctx, int fmt, const int32_t *codes, double *v,
+DRIFT_API int drift_decode(drift_ctx *ctx, int fmt, const int32_t *codes, double *v,
                  int64_t n);
 
 /* Dot.round(x, acc, rm, rng) over an array, element order
  * (java/.../kernel/Dot.java:141-182). acc is DRIFT_ACC_FP16 or _BF16. */
-int drift_acc_round(drift_ctx *ctx, int acc, int rounding, const double *x,
+DRIFT_API int drift_acc_round(drift_ctx *ctx, int acc, int rounding, const double *x,
                     double *y, int64_t n, uint64_t *rng_state);
 
 /* ---------------------------------------------------------- quant layer */
 /* Quant.amax (java/.../kernel/Quant.java:25-34). NaN is ignored. */
-int drift_amax(drift_ctx *ctx, const double *x, int64_t n, double *amax_out);
+DRIFT_API int drift_amax(drift_ctx *ctx, const double *x, int64_t n, double *amax_out);
 
 /* Quant.perTensorScale (java/.../kernel/Quant.java:37-42). Host arithmetic. */
-int drift_per_tensor_scale(int fmt, double amax, double *scale_out);
+DRIFT_API int drift_per_tensor_scale(int fmt, double amax, double *scale_out);
 
 /*
  * Quant.quantize(src, 0, dst, 0, n, f, p, rm, scale, rng)
@@ -161,7 +167,7 @@ int drift_per_tensor_scale(int fmt, double amax, double *scale_out);
  * rng_state may be NULL when no draw is needed; a needed draw with a NULL
  * rng_state is DRIFT_EINVAL (Java: IllegalArgumentException).
  */
-int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt,
+DRIFT_API int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt,
                    int rounding, const double *src, double *dst, int64_t n,
                    double scale, uint64_t *rng_state, int64_t *clamped_out);
 
@@ -178,7 +184,7 @@ int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt,
  * The accumulator rounding may not be STOCHASTIC (DRIFT_EUNSUPPORTED): its
  * random stream is consumed in output order across dots.
  */
-int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N,
+DRIFT_API int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N,
                int64_t K, const double *A, int64_t a_off, int64_t a_row_stride,
                int64_t a_k_stride, const double *B, int64_t b_off,
                int64_t b_row_stride, int64_t b_k_stride, const double *bias,
@@ -186,7 +192,7 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N,
 
 /* ------------------------------------------ device-resident entry points */
 /* As drift_amax; amax lands in the device double *d_amax. */
-int drift_amax_dev(drift_ctx *ctx, const double *d_x, int64_t n,
+DRIFT_API int drift_amax_dev(drift_ctx *ctx, const double *d_x, int64_t n,
                    double *d_amax, void *stream);
 
 /*
@@ -198,26 +204,45 @@ int drift_amax_dev(drift_ctx *ctx, const double *d_x, int64_t n,
  * (NaN into a finite format, a needed draw with d_rng_state NULL) are reported
  * by drift_check_dev.
  */
-int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt,
+DRIFT_API int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt,
                        int rounding, const double *d_src, double *d_dst,
                        int64_t n, const double *d_scale, double scale,
                        uint64_t *d_rng_state, int64_t *d_clamped,
                        void *stream);
 
+/* Quant.perTensorScale (java/.../kernel/Quant.java:37-42) from a device amax
+ * into a device scale, so a cast can follow an amax without a host trip. */
+DRIFT_API int drift_per_tensor_scale_dev(drift_ctx *ctx, int fmt,
+                                         const double *d_amax, double *d_scale,
+                                         void *stream);
+
 /* As drift_gemm on device buffers (offsets folded into the pointers). */
-int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
+DRIFT_API int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
                    int64_t N, int64_t K, const double *d_A,
                    int64_t a_row_stride, int64_t a_k_stride, const double *d_B,
                    int64_t b_row_stride, int64_t b_k_stride,
                    const double *d_bias, double *d_C, int64_t c_row_stride,
                    void *stream);
 
+/* Error sums of RealDotSweep's RMS ratio
+ * (java/.../tools/RealDotSweep.java:245-257): ADDS sum((got-exact)^2) to
+ * d_sums[0] and sum(exact^2) to d_sums[1]. */
+DRIFT_API int drift_error_sums_dev(drift_ctx *ctx, const double *d_got,
+                                   const double *d_exact, int64_t n,
+                                   double *d_sums, void *stream);
+
+/* ----------------------------------------------------------- diagnostics */
+/* No counterpart in the reference: measures the FP64 pipe's DMUL+DADD issue
+ * rate on the context's device (operations per second), the denominator of
+ * the contraction's roofline. Takes a few milliseconds. */
+DRIFT_API int drift_probe_fp64(drift_ctx *ctx, double *ops_per_s);
+
 /*
  * Synchronises `stream` and returns the first device-side error raised since
  * the last check on this context (DRIFT_ENAN_FINITE, DRIFT_EINVAL,
  * DRIFT_ETIMEOUT), clearing it.
  */
-int drift_check_dev(drift_ctx *ctx, void *stream);
+DRIFT_API int drift_check_dev(drift_ctx *ctx, void *stream);
 
 #ifdef __cplusplus
 }

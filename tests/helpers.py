@@ -1,0 +1,45 @@
+"""Test inputs and comparisons shared by the parity tests."""
+from __future__ import annotations
+
+import numpy as np
+
+
+def same_bits(a, b) -> np.ndarray:
+    """Element-wise bit equality of doubles; any NaN equals any NaN (the JVM
+    does not specify NaN payloads, so only NaN-ness is compared)."""
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    both_nan = np.isnan(a) & np.isnan(b)
+    return (a.view(np.int64) == b.view(np.int64)) | both_nan
+
+
+def assert_bits(got, want, what="") -> None:
+    ok = same_bits(got, want)
+    if not ok.all():
+        idx = np.flatnonzero(~ok.reshape(-1))
+        g = np.asarray(got, dtype=np.float64).reshape(-1)
+        w = np.asarray(want, dtype=np.float64).reshape(-1)
+        first = ", ".join(f"[{i}] got {g[i]!r} want {w[i]!r}" for i in idx[:5])
+        raise AssertionError(f"{what}: {idx.size} of {ok.size} differ: {first}")
+
+
+def heavy_tailed(rs: np.random.Generator, n: int, sigma: float = 1.0) -> np.ndarray:
+    """N(0,1) x lognormal(0, sigma), the distribution of the sweeps."""
+    return rs.standard_normal(n) * np.exp(rs.standard_normal(n) * sigma)
+
+
+def with_edges(x: np.ndarray, rs: np.random.Generator, nan: bool = True) -> np.ndarray:
+    """Plants the special values a cast must handle: signed zeros, double
+    subnormals, values far below and above every format, infinities, NaN."""
+    x = x.copy()
+    n = x.size
+    if n < 16:
+        return x
+    specials = [0.0, -0.0, 5e-324, -1e-310, 1e-45, -3e-8, 1e300, -1e300, np.inf, -np.inf,
+                448.0, 449.0, 464.0, 6.0, 7.0, 65504.0, 65520.0]
+    if nan:
+        specials.append(np.nan)
+    pos = rs.choice(n, size=min(n, len(specials) * 3), replace=False)
+    for k, p in enumerate(pos):
+        x[p] = specials[k % len(specials)]
+    return x
