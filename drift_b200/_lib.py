@@ -9,8 +9,12 @@ import ctypes
 import threading
 from pathlib import Path
 
+import os
+
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "libdrift_b200.so"
+# DRIFT_B200_LIB names another build of the same library (for instance one
+# compiled with different tuning flags); by default the in-tree build is used.
+LIB_PATH = Path(os.environ.get("DRIFT_B200_LIB", PKG / "libdrift_b200.so"))
 
 OK, EINVAL, ENAN_FINITE, ECUDA, ETIMEOUT, EUNSUPPORTED, ENOMEM = range(7)
 
@@ -78,7 +82,7 @@ def load() -> ctypes.CDLL:
         if _lib is None:
             from . import build as _build
 
-            if not _build.up_to_date():
+            if LIB_PATH == _build.LIB and not _build.up_to_date():
                 _build.build()
             lib = ctypes.CDLL(str(LIB_PATH))
             for name, (res, args) in SIGNATURES.items():

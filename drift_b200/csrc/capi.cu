@@ -154,8 +154,11 @@ static int enter(drift_ctx *ctx) {
     return DRIFT_OK;
 }
 
+// Device entry points run on the caller's stream exactly as given; NULL is
+// the CUDA default stream, as everywhere in the CUDA runtime.
 static cudaStream_t pick(drift_ctx *ctx, void *stream) {
-    return stream ? (cudaStream_t)stream : ctx->stream;
+    (void)ctx;
+    return (cudaStream_t)stream;
 }
 
 // Reads and clears the device error word; maps it to a status.

@@ -108,8 +108,8 @@ template <> struct AccFmt<DRIFT_ACC_BF16> {
 };
 
 // Dot.round(x, acc, rm, rng), the general form (Dot.java:141-182). The
-// contraction kernel reaches it only when its integer fast path cannot
-// decide (zero, subnormal range, saturation, Inf/NaN).
+// contraction kernel reaches it only when its fast path cannot decide (zero,
+// subnormal range, saturation, Inf/NaN).
 template <int ACC>
 __device__ __noinline__ double acc_round_general(double x, int rm, uint64_t u53, bool &drew) {
     using F = AccFmt<ACC>;
@@ -122,7 +122,7 @@ __device__ __noinline__ double acc_round_general(double x, int rm, uint64_t u53,
     const int q = e - F::mant;
     const double scaled = __dmul_rn(ax, pow2(-q));  // exact
     const double m = round_integral(scaled, rm, u53, drew);
-    double r = q >= -1022 ? __dmul_rn(m, pow2(q)) : m * 0.0;  // q >= -133 always
+    double r = __dmul_rn(m, pow2(q));  // exact below the top binade; q >= -133
     if (r > F::max()) r = F::max();
     return copysign(r, x);
 }
@@ -136,46 +136,107 @@ __device__ __forceinline__ double acc_round_any(int acc, double x, int rm, uint6
 
 // ------------------------------------------------------- fast accumulator rounding
 //
-// The contraction rounds once per multiply-accumulate, so it rounds on the
-// double's bit pattern: for a result that stays a normal number of the target
-// format, rounding to p significant bits is an integer add of (half-ulp - 1 +
-// lsb) followed by clearing the low bits; a carry out of the mantissa bumps
-// the exponent, which is the correct round-up. The result's exponent is then
-// range-checked in two integer ops; anything outside (zero, a subnormal of the
-// target format, overflow, Inf, NaN) is recomputed by the general path.
-// A value below the normal range that the fine rounding lifts to exactly the
-// smallest normal is also right: the coarser subnormal quantum rounds it there
-// too, so the check on the result alone suffices.
+// The contraction rounds once per multiply-accumulate, so the common case
+// must be cheap. For a sum t whose rounded value is a normal number of the
+// accumulator format, rounding to nearest even at a fixed number of
+// significand bits is (t + C) - C with C = 1.5 * 2^(e + SHIFT), e the binade
+// of t and SHIFT = 52 - kept fraction bits: the ulp of C is exactly the
+// target quantum, C is an even multiple of it (so ties go to even), and the
+// subtraction is exact. Building C takes two integer ops on the high word;
+// the two adds run on the FP64 pipe. Truncation clears the low bits.
+//
+// The result is then range-checked on the FP32 pipe: the high word read as a
+// float orders like |r|, so two float compares test 2^min_exp <= |r| <
+// 2^(max_exp+1). Anything outside (zero, the target's subnormal range,
+// overflow, Inf, NaN) is recomputed exactly by the caller. A value just below
+// the normal range that the fine rounding lifts to exactly 2^min_exp is also
+// right: the coarser subnormal quantum rounds it there too, so checking the
+// result alone is enough.
 
-// (float) of a double, returned as the double holding that float
-// (Dot.java:54, :61, :99, :118): round to nearest even at 24 bits.
-__device__ __forceinline__ double round_to_f32(double t) {
-    const uint64_t u = dbits(t);
-    const uint64_t r = (u + 0x0FFFFFFFULL + ((u >> 29) & 1ULL)) & ~0x1FFFFFFFULL;
-    const uint32_t hi2 = (uint32_t)(r >> 32) << 1;  // exponent in bits 21..31
-    if (hi2 - (897u << 21) < (254u << 21)) return bitsd(r);
-    return (double)__double2float_rn(t);
+template <int SHIFT>
+__device__ __forceinline__ double rne_shift(double t) {
+    const int hi = __double2hiint(t);
+    const int chi = ((hi & 0x7FF00000) | 0x00080000) + (SHIFT << 20);
+    const double c = __hiloint2double(chi, 0);
+    return __dsub_rn(__dadd_rn(t, c), c);
 }
 
-// Dot.round for FP16/BF16 with NEAREST_EVEN or TRUNCATE.
-template <int ACC, int RM>
-__device__ __forceinline__ double round_acc_fast(double t) {
-    using F = AccFmt<ACC>;
-    constexpr int P = 52 - F::mant;  // bits below the kept significand
-    constexpr uint64_t low = (1ULL << P) - 1;
-    const uint64_t u = dbits(t);
-    uint64_t r;
-    if (RM == DRIFT_NEAREST_EVEN) {
-        r = (u + (low >> 1) + ((u >> P) & 1ULL)) & ~low;
+template <int SHIFT>
+__device__ __forceinline__ double trunc_shift(double t) {
+    if constexpr (SHIFT >= 32) {
+        return __hiloint2double(__double2hiint(t) & ~((1 << (SHIFT - 32)) - 1), 0);
     } else {
-        r = u & ~low;
+        return __hiloint2double(__double2hiint(t), __double2loint(t) & ~((1 << SHIFT) - 1));
     }
-    constexpr uint32_t lo_e = (uint32_t)(1023 + F::min_exp) << 21;
-    constexpr uint32_t span = (uint32_t)(F::max_exp - F::min_exp + 1) << 21;
-    const uint32_t hi2 = (uint32_t)(r >> 32) << 1;
-    if (hi2 - lo_e < span) return bitsd(r);
-    bool drew;
-    return acc_round_general<ACC>(t, RM, 0, drew);
 }
+
+// lo_e <= biased exponent of r < hi_e, read from the high word on the FP32 pipe.
+template <int LO_E, int HI_E>
+__device__ __forceinline__ bool exp_in_range(double r) {
+    const float f = fabsf(__int_as_float(__double2hiint(r)));
+    return f >= __int_as_float(LO_E << 20) && f < __int_as_float(HI_E << 20);
+}
+
+// Per-accumulator rounding: fast() for the common case, ok() to validate it,
+// exact() for any input (Dot.java:54, :63 and Dot.round, :141-182).
+template <int ACC, int RM> struct AccRound;
+
+template <int RM> struct AccRound<DRIFT_ACC_FP64, RM> {
+    __device__ static double fast(double t) { return t; }
+    __device__ static bool ok(double) { return true; }
+    __device__ static double exact(double t) { return t; }
+};
+
+// (float) of a double, held as the double of that float.
+template <int RM> struct AccRound<DRIFT_ACC_FP32, RM> {
+    __device__ static double fast(double t) { return rne_shift<29>(t); }
+    __device__ static bool ok(double r) { return exp_in_range<1023 - 126, 1023 + 128>(r); }
+    __device__ static double exact(double t) { return (double)__double2float_rn(t); }
+};
+
+// Dot.round for FP16/BF16 under NEAREST_EVEN or TRUNCATE, for any input,
+// inline (no call on the contraction's rare path). Below 2^min_exp the
+// quantum is fixed (2^(min_exp - mant)), so one magic constant serves; above
+// it the binade's own quantum applies; 2^(max_exp+1) and beyond (Inf
+// included) saturate to max; zero and NaN pass through with their sign.
+template <int ACC, int RM>
+__device__ __forceinline__ double narrow_exact(double t) {
+    using F = AccFmt<ACC>;
+    constexpr int S = 52 - F::mant;
+    const double a = fabs(t);
+    const double lo_bound = pow2(F::min_exp);
+    double r;
+    if (!(a >= lo_bound)) {  // below the normal range, or NaN
+        const double c0 = 1.5 * pow2(F::min_exp - F::mant + 52);
+        r = RM == DRIFT_TRUNCATE ? __dsub_rn(__dadd_rz(a, c0), c0) : __dsub_rn(__dadd_rn(a, c0), c0);
+    } else {
+        r = RM == DRIFT_TRUNCATE ? trunc_shift<S>(a) : rne_shift<S>(a);
+        if (a >= pow2(F::max_exp + 1)) r = F::max();
+    }
+    if (r > F::max()) r = F::max();
+    return copysign(r, t);
+}
+
+template <int RM> struct AccRound<DRIFT_ACC_FP16, RM> {
+    using F = AccFmt<DRIFT_ACC_FP16>;
+    __device__ static double fast(double t) {
+        return RM == DRIFT_TRUNCATE ? trunc_shift<52 - F::mant>(t) : rne_shift<52 - F::mant>(t);
+    }
+    __device__ static bool ok(double r) {
+        return exp_in_range<1023 + F::min_exp, 1023 + F::max_exp + 1>(r);
+    }
+    __device__ static double exact(double t) { return narrow_exact<DRIFT_ACC_FP16, RM>(t); }
+};
+
+template <int RM> struct AccRound<DRIFT_ACC_BF16, RM> {
+    using F = AccFmt<DRIFT_ACC_BF16>;
+    __device__ static double fast(double t) {
+        return RM == DRIFT_TRUNCATE ? trunc_shift<52 - F::mant>(t) : rne_shift<52 - F::mant>(t);
+    }
+    __device__ static bool ok(double r) {
+        return exp_in_range<1023 + F::min_exp, 1023 + F::max_exp + 1>(r);
+    }
+    __device__ static double exact(double t) { return narrow_exact<DRIFT_ACC_BF16, RM>(t); }
+};
 
 }  // namespace drift

@@ -8,23 +8,31 @@
 //
 // Per multiply-accumulate: one DMUL and one DADD (never fused: Java rounds the
 // product to double before the add, Dot.java:46/:54/:63) and, for narrow
-// accumulators, the integer rounding of codec.cuh.
+// accumulators, the fast rounding of codec.cuh, validated for eight of a
+// thread's sixteen outputs at a time.
 //
-// Tiling. A CTA of 256 threads owns a 64x64 output tile; each thread owns a
-// 4x4 block (four rows of A, four rows of B). K advances in steps of 16
-// through a double-buffered shared-memory stage: global loads for step t+1
-// are issued into registers before step t is computed. The loader coalesces
-// along whichever operand axis has unit stride, so the strided dgrad/wgrad
-// operands (Pass.java:224, :230) are staged as they lie and the summation
-// order never changes.
+// Tiling. A CTA of 256 threads owns a 64x64 output tile; thread (ty, tx) owns
+// rows ty + 16i and columns tx + 16j (i, j < 4), so the sixteen threads that
+// share a row read sixteen consecutive B rows. K advances in tiles of 16
+// through a 3-stage shared-memory ring laid out [row][k] with a 2-double pad
+// (row stride 144 B), which makes the 16-byte (k, k+1) reads conflict-free.
+// K-contiguous operands with 16-byte-aligned rows are staged with cp.async
+// (LDGSTS, 16 bytes per instruction, zero-filled past the edges); any other
+// strides (the dgrad / wgrad operands, Pass.java:224, :230) go through a
+// register loader into the same layout. The summation order never depends on
+// the staging.
 //
 // Orders. SEQUENTIAL and REVERSED walk k up or down. BLOCKED folds each
-// acc_block chunk into an FP32 (FP64 for FP64 accumulation) total
-// (Dot.java:104-121). PAIRWISE follows a leaf schedule built on the host from
-// the same recursion as Dot.pairwise (half = count >>> 1, leaves of at most 8,
-// Dot.java:86-102): after leaf j the kernel pops and combines merges[j]
-// partial sums from a per-thread stack. The schedule is the same for every
-// output, so the control flow is uniform across the CTA.
+// acc_block chunk into an FP32 total (FP64 for FP64 accumulation,
+// Dot.java:104-121). PAIRWISE follows Dot.pairwise (half = count >>> 1,
+// leaves of at most 8, Dot.java:86-102). When acc_block is a multiple of 16,
+// or K is a power of two >= 16 (every leaf 8 long, every split exact), chunk
+// and leaf boundaries fall on tile boundaries and all segment work happens
+// once per tile: a 16-wide tile is one level-1 node of the pairwise tree and
+// the tiles combine as a perfect binary tree (ctz(t+1) merges after tile t).
+// Other shapes use a leaf schedule built on the host from the same recursion,
+// checked once per k. Either way the schedule is the same for every output,
+// so control flow is uniform across the CTA.
 #include <algorithm>
 #include <vector>
 
@@ -34,7 +42,21 @@
 namespace drift {
 
 constexpr int BM = 64, BN = 64, BK = 16, TM = 4, TN = 4, GEMM_THREADS = 256;
+constexpr int LDK = BK + 2;  // padded row length of a staged tile, in doubles
+constexpr int STAGES = 3;
+constexpr int STAGE_DOUBLES = (BM + BN) * LDK;
+constexpr int GEMM_SMEM = STAGES * STAGE_DOUBLES * (int)sizeof(double);
 constexpr int kMaxPairwiseDepth = 30;  // stack depth; enough for any int32 K
+// Unroll of the k-pair loop of a full tile, chosen by measurement on B200:
+// the narrow accumulators' rounding makes a long tile body fall out of the
+// instruction cache, so they unroll less (pairwise least, as its per-tile
+// merge code is the largest); FP64/FP32 bodies are small and unroll fully.
+template <int ACC, int ORDER>
+constexpr int kp_unroll() {
+    return ORDER == DRIFT_PAIRWISE ? 1 : (ACC == DRIFT_ACC_FP64 || ACC == DRIFT_ACC_FP32) ? 8 : 2;
+}
+
+enum SegMode { SEG_NONE = 0, SEG_TILE = 1, SEG_SCHED = 2 };
 
 struct GemmArgs {
     int64_t M, N, K;
@@ -46,180 +68,295 @@ struct GemmArgs {
     double *C;
     int64_t c_rs;
     int64_t acc_block;
-    const uint8_t *leaf_len;     // PAIRWISE: length of each leaf, in k order
-    const uint8_t *leaf_merges;  // PAIRWISE: combines after each leaf
-    int a_kfast, b_kfast;        // loader coalescing direction
+    const uint8_t *leaf_len;     // SEG_SCHED PAIRWISE: length of each leaf, in k order
+    const uint8_t *leaf_merges;  // SEG_SCHED PAIRWISE: combines after each leaf
+    int a_async, b_async;        // operand staged by cp.async
 };
 
-// s + p rounded as the accumulator does (Dot.java:46, :54, :63).
+// The fast rounding is validated for half of a thread's outputs (two rows of
+// four) at a time: one branch per eight sums keeps the temporaries to eight
+// doubles, and a miss recomputes those eight exactly.
+constexpr int GROUP_ROWS = 2;
+
+// Rounds sixteen sums as the accumulator does (Dot.java:54, :63, :99, :224).
 template <int ACC, int RM>
-__device__ __forceinline__ double acc_add(double s, double p) {
-    const double t = __dadd_rn(s, p);
-    if constexpr (ACC == DRIFT_ACC_FP64) return t;
-    else if constexpr (ACC == DRIFT_ACC_FP32) return round_to_f32(t);
-    else return round_acc_fast<ACC, RM>(t);
+__device__ __forceinline__ void round16(double (&t)[TM][TN]) {
+    using R = AccRound<ACC, RM>;
+    if constexpr (ACC != DRIFT_ACC_FP64) {
+#pragma unroll
+    for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
+        double r[GROUP_ROWS][TN];
+        bool ok = true;
+#pragma unroll
+        for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++) {
+                r[i][j] = R::fast(t[i0 + i][j]);
+                ok = ok & R::ok(r[i][j]);
+            }
+        if (!ok) {
+#pragma unroll
+            for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) r[i][j] = R::exact(t[i0 + i][j]);
+        }
+#pragma unroll
+        for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++) t[i0 + i][j] = r[i][j];
+    }
+    }
 }
 
+// One k step for the thread's 16 outputs: acc = round(acc + a_i * b_j).
 template <int ACC, int RM>
-__device__ __forceinline__ double mac(double s, double a, double b) {
-    return acc_add<ACC, RM>(s, __dmul_rn(a, b));
+__device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[TM],
+                                      const double (&b)[TN]) {
+    using R = AccRound<ACC, RM>;
+    if constexpr (ACC == DRIFT_ACC_FP64) {
+#pragma unroll
+        for (int i = 0; i < TM; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++) acc[i][j] = __dadd_rn(acc[i][j], __dmul_rn(a[i], b[j]));
+    } else {
+#pragma unroll
+        for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
+            double r[GROUP_ROWS][TN];
+            bool ok = true;
+#pragma unroll
+            for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) {
+                    r[i][j] = R::fast(__dadd_rn(acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j])));
+                    ok = ok & R::ok(r[i][j]);
+                }
+            if (!ok) {  // rare: recompute these eight exactly from the same operands
+#pragma unroll
+                for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+                    for (int j = 0; j < TN; j++)
+                        r[i][j] = R::exact(__dadd_rn(acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j])));
+            }
+#pragma unroll
+            for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) acc[i0 + i][j] = r[i][j];
+        }
+    }
 }
 
-// Fold of a BLOCKED chunk into the running total (Dot.java:104-121).
+// Fold of a BLOCKED chunk into the running total (Dot.java:104-121): the
+// total is a float for every accumulator but FP64.
 template <int ACC>
-__device__ __forceinline__ double blocked_fold(double total, double partial) {
-    const double t = __dadd_rn(total, partial);
-    return ACC == DRIFT_ACC_FP64 ? t : round_to_f32(t);
+__device__ __forceinline__ void blocked_fold(double (&tot)[TM][TN], double (&acc)[TM][TN]) {
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const double t = __dadd_rn(tot[i][j], acc[i][j]);
+            tot[i][j] = ACC == DRIFT_ACC_FP64 ? t : (double)__double2float_rn(t);
+            acc[i][j] = 0.0;
+        }
 }
 
-template <int ACC, int ORDER, int RM>
-__global__ void __launch_bounds__(GEMM_THREADS) gemm_kernel(const GemmArgs g) {
-    __shared__ __align__(16) double As[2][BK][BM];
-    __shared__ __align__(16) double Bs[2][BK][BN];
+// Pairwise combine of the stack top with the current node (Dot.java:97-101).
+template <int ACC, int RM>
+__device__ __forceinline__ void combine(const double (&left)[TM][TN], double (&right)[TM][TN]) {
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) right[i][j] = __dadd_rn(left[i][j], right[i][j]);
+    round16<ACC, RM>(right);
+}
+
+__device__ __forceinline__ void cp_async16(double *dst, const double *src, int bytes) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(src), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Stages rows [r0, r0+64) x k [k0, k0+16) of an operand into s[row][k].
+__device__ __forceinline__ void stage_operand(double *s, const double *X, int64_t rows,
+                                              int64_t r0, int64_t rs, int64_t ks, int64_t k0,
+                                              int64_t K, bool async, int tid) {
+    if (async) {
+        // 64 rows x 8 chunks of 16 bytes; two chunks per thread.
+#pragma unroll
+        for (int c = tid; c < 512; c += GEMM_THREADS) {
+            const int row = c >> 3, ch = c & 7;
+            const int64_t r = r0 + row, k = k0 + 2 * ch;
+            int bytes = 0;
+            if (r < rows && k < K) bytes = (K - k >= 2) ? 16 : 8;
+            const double *src = bytes ? X + r * rs + k : X;
+            cp_async16(s + row * LDK + 2 * ch, src, bytes);
+        }
+    } else {
+        const bool kfast = ks == 1 || rs != 1;  // coalesce along the unit stride
+#pragma unroll
+        for (int e = tid; e < BM * BK; e += GEMM_THREADS) {
+            const int kk = kfast ? (e & 15) : (e >> 6);
+            const int rr = kfast ? (e >> 4) : (e & 63);
+            const int64_t r = r0 + rr, k = k0 + kk;
+            s[rr * LDK + kk] = (r < rows && k < K) ? X[r * rs + k * ks] : 0.0;
+        }
+    }
+}
+
+template <int ACC, int ORDER, int RM, int SEG>
+__global__ void __launch_bounds__(GEMM_THREADS, 2) gemm_kernel(const GemmArgs g) {
+    extern __shared__ __align__(16) double smem[];
+    constexpr bool REV = ORDER == DRIFT_REVERSED;
+    constexpr bool PAIR = ORDER == DRIFT_PAIRWISE;
+    constexpr bool BLOCK = ORDER == DRIFT_BLOCKED;
 
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
     const int64_t m0 = (int64_t)blockIdx.y * BM;
     const int64_t n0 = (int64_t)blockIdx.x * BN;
     const int64_t K = g.K;
+    const int64_t T = (K + BK - 1) / BK;
 
-    double acc[TM][TN];
-    double tot[TM][TN];
+    double acc[TM][TN], tot[TM][TN];
 #pragma unroll
     for (int i = 0; i < TM; i++)
 #pragma unroll
         for (int j = 0; j < TN; j++) acc[i][j] = tot[i][j] = 0.0;
-
-    double stk[ORDER == DRIFT_PAIRWISE ? kMaxPairwiseDepth : 1][TM][TN];
+    double stk[PAIR ? kMaxPairwiseDepth : 1][TM][TN];
     int sp = 0;
 
-    const int64_t T = (K + BK - 1) / BK;
-    double ra[4], rb[4];
-
-    auto load_tile = [&](int64_t t) {
-        const int64_t k0 = t * BK;
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const int e = tid + GEMM_THREADS * r;
-            int kk = g.a_kfast ? (e & 15) : (e >> 6);
-            int mm = g.a_kfast ? (e >> 4) : (e & 63);
-            int64_t m = m0 + mm, k = k0 + kk;
-            ra[r] = (m < g.M && k < K) ? g.A[m * g.a_rs + k * g.a_ks] : 0.0;
-            kk = g.b_kfast ? (e & 15) : (e >> 6);
-            mm = g.b_kfast ? (e >> 4) : (e & 63);
-            m = n0 + mm;
-            k = k0 + kk;
-            rb[r] = (m < g.N && k < K) ? g.B[m * g.b_rs + k * g.b_ks] : 0.0;
+    auto issue = [&](int64_t it) {
+        if (it < T) {
+            const int64_t t = REV ? T - 1 - it : it;
+            double *s = smem + (int)(it % STAGES) * STAGE_DOUBLES;
+            stage_operand(s, g.A, g.M, m0, g.a_rs, g.a_ks, t * BK, K, g.a_async, tid);
+            stage_operand(s + BM * LDK, g.B, g.N, n0, g.b_rs, g.b_ks, t * BK, K, g.b_async, tid);
         }
-    };
-    auto store_tile = [&](int buf) {
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const int e = tid + GEMM_THREADS * r;
-            As[buf][g.a_kfast ? (e & 15) : (e >> 6)][g.a_kfast ? (e >> 4) : (e & 63)] = ra[r];
-            Bs[buf][g.b_kfast ? (e & 15) : (e >> 6)][g.b_kfast ? (e >> 4) : (e & 63)] = rb[r];
-        }
+        cp_async_commit();
     };
 
-    // Segment bookkeeping for BLOCKED chunks and PAIRWISE leaves.
-    int64_t seg_left = 0;
-    int64_t leaf = 0;
-    if (ORDER == DRIFT_BLOCKED) seg_left = g.acc_block;
-    if (ORDER == DRIFT_PAIRWISE) seg_left = g.leaf_len[0];
-
-    auto end_segment = [&]() {
-        if (ORDER == DRIFT_BLOCKED) {
+    auto push = [&](int merges) {
+        for (; merges > 0; merges--) {
+            sp--;
+            combine<ACC, RM>(stk[sp], acc);
+        }
 #pragma unroll
-            for (int i = 0; i < TM; i++)
+        for (int i = 0; i < TM; i++)
 #pragma unroll
-                for (int j = 0; j < TN; j++) {
-                    tot[i][j] = blocked_fold<ACC>(tot[i][j], acc[i][j]);
-                    acc[i][j] = 0.0;
-                }
-            seg_left = g.acc_block;
-        } else if (ORDER == DRIFT_PAIRWISE) {
-            int merges = g.leaf_merges[leaf];
-            for (; merges > 0; merges--) {
-                sp--;
-#pragma unroll
-                for (int i = 0; i < TM; i++)
-#pragma unroll
-                    for (int j = 0; j < TN; j++) acc[i][j] = acc_add<ACC, RM>(stk[sp][i][j], acc[i][j]);
+            for (int j = 0; j < TN; j++) {
+                stk[sp][i][j] = acc[i][j];
+                acc[i][j] = 0.0;
             }
-#pragma unroll
-            for (int i = 0; i < TM; i++)
-#pragma unroll
-                for (int j = 0; j < TN; j++) {
-                    stk[sp][i][j] = acc[i][j];
-                    acc[i][j] = 0.0;
-                }
-            sp++;
+        sp++;
+    };
+
+    // SEG_SCHED bookkeeping: the open chunk / leaf and how much of it is left.
+    int64_t seg_left = 0, leaf = 0;
+    if (SEG == SEG_SCHED) seg_left = PAIR ? g.leaf_len[0] : g.acc_block;
+    auto after_k = [&]() {
+        if (SEG != SEG_SCHED || !(PAIR || BLOCK)) return;
+        if (--seg_left != 0) return;
+        if (BLOCK) {
+            blocked_fold<ACC>(tot, acc);
+            seg_left = g.acc_block;
+        } else {
+            push(g.leaf_merges[leaf]);
             leaf++;
             seg_left = g.leaf_len[leaf];  // the schedule carries a sentinel entry
         }
     };
 
-    auto step = [&](int buf, int kk) {
-        const double2 a01 = *reinterpret_cast<const double2 *>(&As[buf][kk][ty * TM]);
-        const double2 a23 = *reinterpret_cast<const double2 *>(&As[buf][kk][ty * TM + 2]);
-        const double2 b01 = *reinterpret_cast<const double2 *>(&Bs[buf][kk][tx * TN]);
-        const double2 b23 = *reinterpret_cast<const double2 *>(&Bs[buf][kk][tx * TN + 2]);
-        const double a[4] = {a01.x, a01.y, a23.x, a23.y};
-        const double b[4] = {b01.x, b01.y, b23.x, b23.y};
-#pragma unroll
-        for (int i = 0; i < TM; i++)
-#pragma unroll
-            for (int j = 0; j < TN; j++) acc[i][j] = mac<ACC, RM>(acc[i][j], a[i], b[j]);
-        if (ORDER == DRIFT_BLOCKED || ORDER == DRIFT_PAIRWISE) {
-            if (--seg_left == 0) end_segment();
-        }
-    };
-
-    if (T > 0) {
-        load_tile(ORDER == DRIFT_REVERSED ? T - 1 : 0);
-        store_tile(0);
-        __syncthreads();
-    }
+    for (int s = 0; s < STAGES - 1; s++) issue(s);
     for (int64_t it = 0; it < T; it++) {
-        const int64_t t = ORDER == DRIFT_REVERSED ? T - 1 - it : it;
-        const int buf = (int)(it & 1);
-        if (it + 1 < T) load_tile(ORDER == DRIFT_REVERSED ? t - 1 : t + 1);
+        cp_async_wait<STAGES - 2>();
+        __syncthreads();
+        issue(it + STAGES - 1);
+        const int64_t t = REV ? T - 1 - it : it;
+        const double *sA = smem + (int)(it % STAGES) * STAGE_DOUBLES;
+        const double *sB = sA + BM * LDK;
         const int kn = (int)(K - t * BK < BK ? K - t * BK : BK);
-        if (ORDER == DRIFT_REVERSED) {
-            if (kn == BK) {
+
+        if (SEG != SEG_SCHED && kn == BK) {
+            // A full tile, no per-k segment work: two k per 16-byte read.
+            double leaf0[PAIR ? TM : 1][PAIR ? TN : 1];
+            constexpr int kUnroll = kp_unroll<ACC, ORDER>();
+#pragma unroll kUnroll
+            for (int q = 0; q < BK / 2; q++) {
+                const int kp = REV ? BK / 2 - 1 - q : q;
+                double2 a2[TM], b2[TN];
 #pragma unroll
-                for (int kk = BK - 1; kk >= 0; kk--) step(buf, kk);
-            } else {
-                for (int kk = kn - 1; kk >= 0; kk--) step(buf, kk);
+                for (int i = 0; i < TM; i++)
+                    a2[i] = *reinterpret_cast<const double2 *>(sA + (ty + 16 * i) * LDK + 2 * kp);
+#pragma unroll
+                for (int j = 0; j < TN; j++)
+                    b2[j] = *reinterpret_cast<const double2 *>(sB + (tx + 16 * j) * LDK + 2 * kp);
+                const double ax[TM] = {a2[0].x, a2[1].x, a2[2].x, a2[3].x};
+                const double ay[TM] = {a2[0].y, a2[1].y, a2[2].y, a2[3].y};
+                const double bx[TN] = {b2[0].x, b2[1].x, b2[2].x, b2[3].x};
+                const double by[TN] = {b2[0].y, b2[1].y, b2[2].y, b2[3].y};
+                if (REV) {
+                    mac16<ACC, RM>(acc, ay, by);
+                    mac16<ACC, RM>(acc, ax, bx);
+                } else {
+                    mac16<ACC, RM>(acc, ax, bx);
+                    mac16<ACC, RM>(acc, ay, by);
+                }
+                if constexpr (PAIR && SEG == SEG_TILE) {
+                    if (q == BK / 4 - 1) {  // end of the tile's first leaf of 8
+#pragma unroll
+                        for (int i = 0; i < TM; i++)
+#pragma unroll
+                            for (int j = 0; j < TN; j++) {
+                                leaf0[i][j] = acc[i][j];
+                                acc[i][j] = 0.0;
+                            }
+                    }
+                }
+            }
+            if constexpr (SEG == SEG_TILE && PAIR) {
+                combine<ACC, RM>(leaf0, acc);      // the tile's level-1 node
+                push(__ffsll(t + 1) - 1);          // ctz(t+1) merges in a perfect tree
+            } else if constexpr (SEG == SEG_TILE && BLOCK) {
+                if (((t + 1) * BK) % g.acc_block == 0) blocked_fold<ACC>(tot, acc);
             }
         } else {
-            if (kn == BK) {
+            // Partial tile, or per-k segment bookkeeping.
+#pragma unroll 1
+            for (int q = 0; q < kn; q++) {
+                const int kk = REV ? kn - 1 - q : q;
+                double a[TM], b[TN];
 #pragma unroll
-                for (int kk = 0; kk < BK; kk++) step(buf, kk);
-            } else {
-                for (int kk = 0; kk < kn; kk++) step(buf, kk);
+                for (int i = 0; i < TM; i++) a[i] = sA[(ty + 16 * i) * LDK + kk];
+#pragma unroll
+                for (int j = 0; j < TN; j++) b[j] = sB[(tx + 16 * j) * LDK + kk];
+                mac16<ACC, RM>(acc, a, b);
+                after_k();
             }
         }
-        if (it + 1 < T) {
-            store_tile(buf ^ 1);
-            __syncthreads();
-        }
     }
+    cp_async_wait<0>();
 
     // A BLOCKED chunk still open at the end is folded like the others.
-    if (ORDER == DRIFT_BLOCKED && seg_left != g.acc_block) end_segment();
+    if (BLOCK) {
+        const bool open = SEG == SEG_SCHED ? seg_left != g.acc_block : (K % g.acc_block) != 0;
+        if (open) blocked_fold<ACC>(tot, acc);
+    }
 
 #pragma unroll
     for (int i = 0; i < TM; i++) {
-        const int64_t m = m0 + ty * TM + i;
+        const int64_t m = m0 + ty + 16 * i;
         if (m >= g.M) continue;
 #pragma unroll
         for (int j = 0; j < TN; j++) {
-            const int64_t n = n0 + tx * TN + j;
+            const int64_t n = n0 + tx + 16 * j;
             if (n >= g.N) continue;
             double v;
-            if (ORDER == DRIFT_BLOCKED) v = tot[i][j];
-            else if (ORDER == DRIFT_PAIRWISE) v = K > 0 ? stk[0][i][j] : 0.0;
+            if (BLOCK) v = tot[i][j];
+            else if (PAIR) v = K > 0 ? stk[0][i][j] : 0.0;
             else v = acc[i][j];
             if (g.bias) v = __dadd_rn(v, g.bias[n]);  // Pass.java:202
             g.C[m * g.c_rs + n] = v;
@@ -230,7 +367,7 @@ __global__ void __launch_bounds__(GEMM_THREADS) gemm_kernel(const GemmArgs g) {
 // ------------------------------------------------------------------ schedule
 
 // Leaf lengths and post-leaf merge counts of Dot.pairwise over `count` terms
-// (Dot.java:86-102), in k order, plus the stack depth the walk reaches.
+// (Dot.java:86-102), in k order.
 static void pairwise_walk(int64_t count, std::vector<uint8_t> &len, std::vector<uint8_t> &merges) {
     if (count <= 8) {
         len.push_back((uint8_t)count);
@@ -263,21 +400,33 @@ int pairwise_schedule(int64_t K, std::vector<uint8_t> &sched, int *depth) {
 
 // ------------------------------------------------------------------ launcher
 
-template <int ACC, int ORDER, int RM>
-static void launch_one(const GemmArgs &g, dim3 grid, cudaStream_t st) {
-    gemm_kernel<ACC, ORDER, RM><<<grid, GEMM_THREADS, 0, st>>>(g);
+template <int ACC, int ORDER, int RM, int SEG>
+static int launch_one(const GemmArgs &g, dim3 grid, cudaStream_t st) {
+    // The shared-memory opt-in is per device; setting it is a cheap host call.
+    if (cudaFuncSetAttribute(gemm_kernel<ACC, ORDER, RM, SEG>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM) != cudaSuccess)
+        return DRIFT_ECUDA;
+    gemm_kernel<ACC, ORDER, RM, SEG><<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(g);
+    return DRIFT_OK;
 }
 
 template <int ACC, int RM>
-static int launch_order(int order, const GemmArgs &g, dim3 grid, cudaStream_t st) {
+static int launch_order(int order, int seg, const GemmArgs &g, dim3 grid, cudaStream_t st) {
     switch (order) {
-        case DRIFT_SEQUENTIAL: launch_one<ACC, DRIFT_SEQUENTIAL, RM>(g, grid, st); break;
-        case DRIFT_REVERSED: launch_one<ACC, DRIFT_REVERSED, RM>(g, grid, st); break;
-        case DRIFT_PAIRWISE: launch_one<ACC, DRIFT_PAIRWISE, RM>(g, grid, st); break;
-        case DRIFT_BLOCKED: launch_one<ACC, DRIFT_BLOCKED, RM>(g, grid, st); break;
+        case DRIFT_SEQUENTIAL: return launch_one<ACC, DRIFT_SEQUENTIAL, RM, SEG_NONE>(g, grid, st);
+        case DRIFT_REVERSED: return launch_one<ACC, DRIFT_REVERSED, RM, SEG_NONE>(g, grid, st);
+        case DRIFT_PAIRWISE:
+            return seg == SEG_TILE ? launch_one<ACC, DRIFT_PAIRWISE, RM, SEG_TILE>(g, grid, st)
+                                   : launch_one<ACC, DRIFT_PAIRWISE, RM, SEG_SCHED>(g, grid, st);
+        case DRIFT_BLOCKED:
+            return seg == SEG_TILE ? launch_one<ACC, DRIFT_BLOCKED, RM, SEG_TILE>(g, grid, st)
+                                   : launch_one<ACC, DRIFT_BLOCKED, RM, SEG_SCHED>(g, grid, st);
         default: return DRIFT_EINVAL;
     }
-    return DRIFT_OK;
+}
+
+static bool async_ok(const double *X, int64_t rs, int64_t ks) {
+    return ks == 1 && (rs % 2) == 0 && ((uintptr_t)X % 16) == 0;
 }
 
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
@@ -309,29 +458,37 @@ int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int6
     g.C = C;
     g.c_rs = c_rs;
     g.acc_block = std::max<int64_t>(1, p->acc_block);  // Dot.java:105
-    // Coalesce along k when k has unit stride or rows do not.
-    g.a_kfast = (a_ks == 1 || a_rs != 1) ? 1 : 0;
-    g.b_kfast = (b_ks == 1 || b_rs != 1) ? 1 : 0;
+    g.a_async = async_ok(A, a_rs, a_ks);
+    g.b_async = async_ok(B, b_rs, b_ks);
+    int seg = SEG_NONE;
+    if (p->order == DRIFT_BLOCKED) seg = (g.acc_block % BK == 0) ? SEG_TILE : SEG_SCHED;
     if (p->order == DRIFT_PAIRWISE) {
-        const uint8_t *d = cache.get(K, st);
-        if (!d) return cache.last_status();
-        g.leaf_len = d;
-        g.leaf_merges = d + cache.leaves(K) + 1;
+        seg = (K >= 16 && (K & (K - 1)) == 0) ? SEG_TILE : SEG_SCHED;
+        if (seg == SEG_SCHED) {
+            const uint8_t *d = cache.get(K, st);
+            if (!d) return cache.last_status();
+            g.leaf_len = d;
+            g.leaf_merges = d + cache.leaves(K) + 1;
+        }
     }
     const dim3 grid((unsigned)gx, (unsigned)gy);
     int rc;
     switch (p->acc) {
-        case DRIFT_ACC_FP64: rc = launch_order<DRIFT_ACC_FP64, DRIFT_NEAREST_EVEN>(p->order, g, grid, st); break;
-        case DRIFT_ACC_FP32: rc = launch_order<DRIFT_ACC_FP32, DRIFT_NEAREST_EVEN>(p->order, g, grid, st); break;
+        case DRIFT_ACC_FP64:
+            rc = launch_order<DRIFT_ACC_FP64, DRIFT_NEAREST_EVEN>(p->order, seg, g, grid, st);
+            break;
+        case DRIFT_ACC_FP32:
+            rc = launch_order<DRIFT_ACC_FP32, DRIFT_NEAREST_EVEN>(p->order, seg, g, grid, st);
+            break;
         case DRIFT_ACC_FP16:
             rc = p->acc_rounding == DRIFT_TRUNCATE
-                     ? launch_order<DRIFT_ACC_FP16, DRIFT_TRUNCATE>(p->order, g, grid, st)
-                     : launch_order<DRIFT_ACC_FP16, DRIFT_NEAREST_EVEN>(p->order, g, grid, st);
+                     ? launch_order<DRIFT_ACC_FP16, DRIFT_TRUNCATE>(p->order, seg, g, grid, st)
+                     : launch_order<DRIFT_ACC_FP16, DRIFT_NEAREST_EVEN>(p->order, seg, g, grid, st);
             break;
         default:
             rc = p->acc_rounding == DRIFT_TRUNCATE
-                     ? launch_order<DRIFT_ACC_BF16, DRIFT_TRUNCATE>(p->order, g, grid, st)
-                     : launch_order<DRIFT_ACC_BF16, DRIFT_NEAREST_EVEN>(p->order, g, grid, st);
+                     ? launch_order<DRIFT_ACC_BF16, DRIFT_TRUNCATE>(p->order, seg, g, grid, st)
+                     : launch_order<DRIFT_ACC_BF16, DRIFT_NEAREST_EVEN>(p->order, seg, g, grid, st);
     }
     if (rc) return rc;
     return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;

@@ -16,8 +16,8 @@
  *    arrays). They copy to the device, run, copy back, and return only when
  *    the result is in the caller's buffer. They never keep a pointer.
  *  - *_dev entry points take DEVICE pointers and a cudaStream_t passed as
- *    void* (NULL = the context's own stream). They are asynchronous unless
- *    noted.
+ *    void*, used as given (NULL is the CUDA default stream). They are
+ *    asynchronous with respect to the host unless noted.
  *  - rng_state is the Java Rng.state() long (java/src/main/java/io/drift/fmt/
  *    Rng.java:29-31). On return it holds the state the Java Rng would hold
  *    after the same calls, so callers can interleave engine calls with Java
