@@ -466,6 +466,20 @@ int drift_probe_fp64(drift_ctx *ctx, double *ops_per_s) {
     return rc ? fail(rc, "fp64 probe") : DRIFT_OK;
 }
 
+int drift_quantize_dev_noalloc(const drift_policy *p, int fmt, int rounding, const double *d_src,
+                               double *d_dst, int64_t n, const double *d_scale, double scale,
+                               uint64_t *d_rng_state, int64_t *d_clamped, int *d_err,
+                               void *stream) {
+    if (!p || !d_err || n < 0 || (n > 0 && (!d_src || !d_dst)))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    const int rc = launch_quantize_noalloc(p, fmt, rounding, d_src, d_dst, n, d_scale, scale,
+                                           d_rng_state, (unsigned long long *)d_clamped, d_err,
+                                           (cudaStream_t)stream);
+    if (rc == DRIFT_ENOMEM)
+        return fail(rc, "too many items for the fixed scratch array (DRIFT_NOALLOC_MAX_ITEMS)");
+    return rc ? fail(rc, "no-allocation quantize launch") : DRIFT_OK;
+}
+
 int drift_check_dev(drift_ctx *ctx, void *stream) {
     int rc = enter(ctx);
     if (rc) return rc;

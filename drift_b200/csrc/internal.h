@@ -50,6 +50,10 @@ int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const
                     double *d_dst, int64_t n, const double *d_scale, double scale,
                     uint64_t *d_state, unsigned long long *d_clamped, int *d_err,
                     cudaStream_t st);
+int launch_quantize_noalloc(const drift_policy *p, int fmt, int rm, const double *d_src,
+                            double *d_dst, int64_t n, const double *d_scale, double scale,
+                            uint64_t *d_state, unsigned long long *d_clamped, int *d_err,
+                            cudaStream_t st);
 int launch_encode(Workspace &ws, int fmt, int rm, const double *d_v, int32_t *d_codes, int64_t n,
                   uint64_t *d_state, int *d_err, cudaStream_t st);
 int launch_decode(int fmt, const int32_t *d_codes, double *d_v, int64_t n, cudaStream_t st);

@@ -19,6 +19,7 @@
 // and the apply pass recomputes each element's rank from the item counts and
 // a warp ballot. No kernel waits on another CTA, so nothing can spin.
 #include <cstdio>
+#include <mutex>
 
 #include "codec.cuh"
 #include "internal.h"
@@ -432,6 +433,95 @@ int launch_acc_round(Workspace &ws, int acc, int rm, const double *d_x, double *
     if ((acc != DRIFT_ACC_FP16 && acc != DRIFT_ACC_BF16) || rm < 0 || rm > 2) return DRIFT_EINVAL;
     AccRoundOp op{d_x, d_y, acc, rm};
     return run_elem(ws, op, n, 32, rm == DRIFT_STOCHASTIC, d_state, nullptr, d_err, st);
+}
+
+// ------------------------------------------------------------------ no-allocation cast
+//
+// A second entry to the same cast passes for callers that must not allocate
+// device memory while they run. The stochastic passes need scratch (draw
+// counts per item and per CTA, and the Rng state before the call); here it
+// lives in one fixed array in this file instead of a growable workspace, so a
+// call never allocates or frees anything. The array is a device symbol: host
+// code may not use its name as an address, so on the first call on each
+// device (with that device current) its device address is looked up with
+// cudaGetSymbolAddress and cached.
+//
+// Every call on a device shares the array and it keeps the last call's
+// contents; the count pass writes every entry the apply pass reads, so nothing
+// needs clearing between calls. Two calls that overlap on the GPU (different
+// streams, or different host threads on one device) race on it.
+
+constexpr int64_t kNoAllocCtas = (DRIFT_NOALLOC_MAX_ITEMS + kItemsPerCta - 1) / kItemsPerCta;
+constexpr size_t kNoAllocBytes =
+    (size_t)kNoAllocCtas * sizeof(uint64_t) + 256 + (size_t)kNoAllocCtas * kItemsPerCta * sizeof(uint32_t);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+static constexpr int kNoAllocMaxDevices = 64;
+static void *g_noalloc_addr[kNoAllocMaxDevices];
+static std::mutex g_noalloc_mutex;
+
+// Device address of this device's copy of the scratch array (looked up once).
+static int noalloc_scratch(char **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return DRIFT_ECUDA;
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return DRIFT_EUNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return DRIFT_ECUDA;
+        g_noalloc_addr[dev] = p;
+    }
+    *out = (char *)g_noalloc_addr[dev];
+    return DRIFT_OK;
+}
+
+int launch_quantize_noalloc(const drift_policy *p, int fmt, int rm, const double *d_src,
+                            double *d_dst, int64_t n, const double *d_scale, double scale,
+                            uint64_t *d_state, unsigned long long *d_clamped, int *d_err,
+                            cudaStream_t st) {
+    if (n < 0) return DRIFT_EINVAL;
+    if (fmt == DRIFT_FMT_NONE) {  // Quant.java:58-61: a plain copy
+        if (n && d_dst != d_src &&
+            cudaMemcpyAsync(d_dst, d_src, n * sizeof(double), cudaMemcpyDeviceToDevice, st) !=
+                cudaSuccess)
+            return DRIFT_ECUDA;
+        return DRIFT_OK;
+    }
+    QuantOp op;
+    if (!fmt_desc(fmt, &op.f)) return DRIFT_EINVAL;
+    if (rm < 0 || rm > 2) return DRIFT_EINVAL;
+    if (p->scaling < 0 || p->scaling > 2) return DRIFT_EINVAL;
+    if (p->scaling == DRIFT_MX_BLOCK && p->scale_block <= 0) return DRIFT_EINVAL;
+    const int64_t item_len = p->scaling == DRIFT_MX_BLOCK ? p->scale_block : 32;
+    const int64_t items = (n + item_len - 1) / item_len;
+    if (items > DRIFT_NOALLOC_MAX_ITEMS) return DRIFT_ENOMEM;
+    if (n == 0) return DRIFT_OK;
+    op.src = d_src;
+    op.dst = d_dst;
+    op.rm = rm;
+    op.scaling = p->scaling;
+    op.headroom = p->mx_headroom;
+    op.d_scale = p->scaling == DRIFT_PER_TENSOR ? d_scale : nullptr;
+    op.scale = scale;
+    op.inv = 1.0 / scale;
+    const int64_t grid = (items + kItemsPerCta - 1) / kItemsPerCta;
+    SrArgs sr{nullptr, nullptr, nullptr, d_clamped, d_err};
+    if (rm != DRIFT_STOCHASTIC) {
+        elem_kernel<QuantOp, 0><<<(unsigned)grid, kThreads, 0, st>>>(op, n, item_len, sr);
+        return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+    }
+    char *base = nullptr;
+    const int rc = noalloc_scratch(&base);
+    if (rc) return rc;
+    sr.cta_counts = (uint64_t *)base;
+    uint64_t *state_before = (uint64_t *)(base + (size_t)kNoAllocCtas * sizeof(uint64_t));
+    sr.item_counts = (uint32_t *)(base + (size_t)kNoAllocCtas * sizeof(uint64_t) + 256);
+    sr.state_before = state_before;
+    elem_kernel<QuantOp, 1><<<(unsigned)grid, kThreads, 0, st>>>(op, n, item_len, sr);
+    sr_scan_kernel<<<1, 1024, 0, st>>>(sr.cta_counts, grid, d_state, state_before, d_err);
+    elem_kernel<QuantOp, 2><<<(unsigned)grid, kThreads, 0, st>>>(op, n, item_len, sr);
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 
 }  // namespace drift

@@ -216,6 +216,39 @@ DRIFT_API int drift_per_tensor_scale_dev(drift_ctx *ctx, int fmt,
                                          const double *d_amax, double *d_scale,
                                          void *stream);
 
+/*
+ * drift_quantize_dev for callers that cannot allocate device memory. No
+ * counterpart in the reference: it exists for host programs that reserve all
+ * device memory up front under a fixed budget and do not let a library
+ * allocate while they run (a cudaMalloc can fail once the budget is spent, and
+ * cudaMalloc/cudaFree synchronise the device, stalling the caller's other
+ * streams). It takes no drift_ctx, since opening one allocates.
+ *
+ * The cast is the same as drift_quantize_dev's, bit for bit. Stochastic
+ * rounding needs scratch space; it comes from one array of about 1 MiB that
+ * the library declares statically, which every GPU that loads the library
+ * holds until the process exits. That bounds one call to
+ * DRIFT_NOALLOC_MAX_ITEMS items (groups of 32 elements, or MX blocks of
+ * scale_block elements): n up to 8,388,608 elements for an element-wise cast
+ * with 32-element items. Larger calls return DRIFT_ENOMEM and do nothing.
+ *
+ * The first call on each device looks up the array's device address with
+ * that device current; make that first call before any stream capture. All
+ * calls share the array, so calls that overlap on the GPU (other streams, or
+ * other threads on the same device) race and must be serialised by the
+ * caller. Device-side errors (NaN into a format without NaN, a needed draw
+ * with d_rng_state NULL) are ORed into the caller's device int *d_err, which
+ * the caller clears and reads. Nothing is allocated or freed by the call.
+ */
+#define DRIFT_NOALLOC_MAX_ITEMS (1 << 18)
+DRIFT_API int drift_quantize_dev_noalloc(const drift_policy *p, int fmt,
+                                         int rounding, const double *d_src,
+                                         double *d_dst, int64_t n,
+                                         const double *d_scale, double scale,
+                                         uint64_t *d_rng_state,
+                                         int64_t *d_clamped, int *d_err,
+                                         void *stream);
+
 /* As drift_gemm on device buffers (offsets folded into the pointers). */
 DRIFT_API int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
                    int64_t N, int64_t K, const double *d_A,
