@@ -431,6 +431,43 @@ def run_reference(args):
     return 0
 
 
+def run_kernels(args):
+    """Per-policy contraction timing at one size (also the command ncu profiles):
+    each selected policy's GEMM runs once to warm up, then `--steps` times under
+    CUDA events on the launching stream."""
+    import torch
+    import drift_b200 as d
+
+    S = args.size
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    A = (torch.randn(S, S, device=dev, generator=g) *
+         torch.exp(torch.randn(S, S, device=dev, generator=g))).double()
+    B = (torch.randn(S, S, device=dev, generator=g) *
+         torch.exp(torch.randn(S, S, device=dev, generator=g))).double()
+    C = torch.empty_like(A)
+    pols = [d.NumericPolicy.exact()] + sweep_policies(d)
+    if args.policies:
+        keep = [x.strip() for x in args.policies.split(",")]
+        pols = [p for p in pols if p.name in keep]
+    stream = torch.cuda.current_stream()
+    out = {}
+    for p in pols:
+        d.gemm_dev(p, A, B, C)
+        if args.steps > 0:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                d.gemm_dev(p, A, B, C)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            out[p.name] = args.steps * S ** 3 / (e0.elapsed_time(e1) * 1e-3)
+    d.check_dev()
+    print(json.dumps({"mode": "kernels", "size": S, "mac_per_s": out}), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -442,11 +479,16 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
+    ap.add_argument("--mode", choices=["sweep", "kernels"], default="sweep",
+                    help="kernels: time each policy's contraction alone (for profiling)")
+    ap.add_argument("--policies", default="", help="kernels mode: comma-separated policy names")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "engine":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         return run_reference(args)
+    if args.mode == "kernels":
+        return run_kernels(args)
     return run_engine(args)
 
 
