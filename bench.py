@@ -180,18 +180,15 @@ def run_engine(args):
     import torch
     import drift_b200 as d
 
+    from drift_b200 import dist as ddist
+
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
     d.Context.use_device(local)
     ctx = d.Context.current()
     pg = None
     if world > 1:
-        import datetime
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
-        pg = dist
+        pg = ddist.init("nccl", timeout_s=600, device=torch.device("cuda", local))
     stream = torch.cuda.current_stream()
     S = args.size
     M = N = K = S
@@ -208,21 +205,22 @@ def run_engine(args):
         y *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float32))
         return x.double(), y.double()
 
-    A, B = make_inputs(rank)
+    seed = ddist.seeds_for(rank, world, 0)[0]  # this rank's seed, the same every step
+    A, B = make_inputs(seed)
     qA = torch.empty_like(A)
     qB = torch.empty_like(B)
     C = torch.empty((M, N), dtype=torch.float64, device=dev)
     Cx = torch.empty((M, N), dtype=torch.float64, device=dev)
     n_pol = len(pols)
     sums = torch.zeros((n_pol, 2), dtype=torch.float64, device=dev)
-    clamps = torch.zeros((n_pol,), dtype=torch.int64, device=dev)
+    clamps = torch.zeros((n_pol, 2), dtype=torch.int64, device=dev)  # clamps in A, in B
     scal = torch.zeros((4,), dtype=torch.float64, device=dev)  # amax A, amax B, scale A, scale B
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(n_pol + 1)]
     gemm_ms = [0.0] * (n_pol + 1)
     launches = [0]
 
-    def cast(p, src, dst, slot, clamp_slot):
+    def cast(p, src, dst, slot, counter):
         f = p.input_format
         if f is None:
             return src
@@ -230,11 +228,10 @@ def run_engine(args):
             d.amax_dev(src, scal[slot:slot + 1], ctx=ctx)
             d.per_tensor_scale_dev(f, scal[slot:slot + 1], scal[2 + slot:3 + slot], ctx=ctx)
             d.quantize_dev(p, f, p.input_rounding, src, dst, d_scale=scal[2 + slot:3 + slot],
-                           d_clamped=clamps[clamp_slot:clamp_slot + 1], ctx=ctx)
+                           d_clamped=counter, ctx=ctx)
             launches[0] += 3
         else:
-            d.quantize_dev(p, f, p.input_rounding, src, dst,
-                           d_clamped=clamps[clamp_slot:clamp_slot + 1], ctx=ctx)
+            d.quantize_dev(p, f, p.input_rounding, src, dst, d_clamped=counter, ctx=ctx)
             launches[0] += 1
         return dst
 
@@ -244,16 +241,14 @@ def run_engine(args):
         ev[0][1].record(stream)
         launches[0] += 1
         for k, p in enumerate(pols):
-            a = cast(p, A, qA, 0, k)
-            b = cast(p, B, qB, 1, k)
+            a = cast(p, A, qA, 0, clamps[k, 0:1])
+            b = cast(p, B, qB, 1, clamps[k, 1:2])
             ev[k + 1][0].record(stream)
             d.gemm_dev(p, a, b, C, ctx=ctx)
             ev[k + 1][1].record(stream)
             d.error_sums_dev(C, Cx, sums[k], ctx=ctx)
             launches[0] += 2
-        if pg is not None:
-            pg.all_reduce(sums)
-            pg.all_reduce(clamps)
+        ddist.reduce_stats(sums, clamps, pg)
 
     def barrier():
         torch.cuda.synchronize()
@@ -281,11 +276,7 @@ def run_engine(args):
     for k in range(n_pol + 1):
         gemm_ms[k] = ev[k][0].elapsed_time(ev[k][1])
     d.check_dev(ctx=ctx)
-    ms = t_start.elapsed_time(t_end)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if pg is not None:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = ddist.max_over_ranks(t_start.elapsed_time(t_end), pg, dev)
     macs_per_step_rank = (n_pol + 1) * M * N * K
     value = macs_per_step_rank * world * args.steps / (ms_max * 1e-3)
 
@@ -302,8 +293,11 @@ def run_engine(args):
     # Statistics (summed over ranks): RMS ratio and clamps per pair.
     s = sums.cpu().numpy()
     c = clamps.cpu().numpy()
-    stats = {p.name: {"rms_error_ratio": float(np.sqrt(s[k, 0] / s[k, 1])),
-                      "clamped_per_pair": float(c[k]) / (args.steps * world * M * N)}
+    stats = {p.name: {"rms_error_ratio": ddist.rms_ratio(float(s[k, 0]), float(s[k, 1])),
+                      # DotSweep's clamps per pair (DotSweep.java:119-120): clamps in
+                      # row i of A plus clamps in row j of B, averaged over all pairs.
+                      "clamped_per_pair": (float(c[k, 0]) / M + float(c[k, 1]) / N)
+                      / (args.steps * world)}
              for k, p in enumerate(pols)}
 
     e2e = None
@@ -315,9 +309,7 @@ def run_engine(args):
         v, cores, desc = cpu_baseline(S, args.cpu_budget)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}
 
-    if pg is not None:
-        pg.barrier()
-        pg.destroy_process_group()
+    ddist.finish(pg)
     if rank != 0:
         return 0
     line = {
@@ -327,7 +319,7 @@ def run_engine(args):
         "data": "synthetic: N(0,1) x lognormal(0,1) fp32 values held in doubles, seeded per rank",
         "config": {"workload": f"policy sweep GEMM M=N=K={S}, 12 policies + exact FP64, "
                                f"1 seed per rank per step", "M": M, "N": N, "K": K,
-                   "policies": [p.name for p in pols], "seeds_per_step": world,
+                   "policies": [p.name for p in pols], "seeds_per_step": world, "seed_of_rank_0": 0,
                    "l2": "inputs (2 x 512 MiB at 8192) are larger than L2",
                    "parallelism": f"shard by seed x{world}"},
         "roofline": {"bound": "fp64", "achieved": achieved / 1e12, "peak": fp64_peak / 1e12,
@@ -391,10 +383,9 @@ def run_e2e(d, args, A, B, pols, exact_p, world, rank, pg):
     for _ in range(steps):
         one_step()
     dt = time.perf_counter() - t0
-    tt = torch.tensor([dt], dtype=torch.float64, device="cuda")
-    if pg is not None:
-        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
-    dt = float(tt.item())
+    from drift_b200 import dist as ddist
+
+    dt = ddist.max_over_ranks(dt, pg, torch.device("cuda", torch.cuda.current_device()))
     macs = (len(pols) + 1) * S ** 3 * world * steps
     return {"value": macs / dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "steps": steps, "path": "drift_quantize/drift_amax/drift_gemm on pinned host buffers"}
