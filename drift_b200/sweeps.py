@@ -1,0 +1,240 @@
+"""Drivers of the reference's dot-product studies on the engine.
+
+dot_sweep       DotSweep (java/src/main/java/io/drift/tools/DotSweep.java): many
+                seeds x lengths x policies, the median relative error per
+                (policy, length) and the clamps per vector pair.
+real_dot_batch  RealDotSweep (java/src/main/java/io/drift/tools/RealDotSweep.java):
+                4096 windows x 64 units of 2048 terms on synthetic tensors, the
+                true median relative error and the RMS ratio per policy.
+mx_gemm         The block-scaled GEMM study: e4m3 / e2m1 operands under per-tensor
+                and MX (spec and +1) scaling, FP32 sequential accumulation, with
+                clamps per vector pair and per block pair and the relative error.
+
+Inputs are synthetic (seeded): N(0,1) x lognormal(0, sigma) vectors, windows
+of an N(0,1) embedding table, and Kaiming-normal weights. Every cast and dot
+runs in the engine; the statistics are order statistics and sums of the
+bit-exact outputs.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+
+from .fmt import Formats, Rng, Rounding
+from .kernel import Acc, NumericPolicy, Order, Quant, Scaling, gemm
+
+
+def heavy_tailed(rs: np.random.Generator, n: int, sigma: float = 1.0, fp32: bool = True):
+    """N(0,1) x lognormal(0, sigma); held as fp32 values when fp32 is set."""
+    x = rs.standard_normal(n) * np.exp(rs.standard_normal(n) * sigma)
+    return x.astype(np.float32).astype(np.float64) if fp32 else x
+
+
+def dot_sweep_policies() -> List[NumericPolicy]:
+    """The dot-sweep configuration: FP32/FP16/BF16 accumulators x sequential /
+    pairwise / blocked-32 on uncast inputs, plus an e4m3 per-tensor cast with
+    FP32 sequential accumulation (a subset of DotSweep.cases, DotSweep.java:66-106)."""
+    b = NumericPolicy.builder
+    ps = []
+    for acc in (Acc.FP32, Acc.FP16, Acc.BF16):
+        for o in (Order.SEQUENTIAL, Order.PAIRWISE, Order.BLOCKED):
+            ps.append(b(f"{acc.name.lower()} {o.name.lower()}").acc(acc).order(o).acc_block(32).build())
+    ps.append(b("e4m3 per-tensor").input(Formats.E4M3).scaling(Scaling.PER_TENSOR).build())
+    return ps
+
+
+@dataclass
+class DotResult:
+    value: float
+    clamped: int
+
+
+def dot_run(p: NumericPolicy, a: np.ndarray, b: np.ndarray, seed: int) -> DotResult:
+    """DotSweep.run (DotSweep.java:112-122): its own Rng, per-tensor scales of
+    each vector, cast a then b on the shared Rng, one dot."""
+    n = a.size
+    rng = Rng(0xD1F7 + seed)
+    f = p.input_format
+    sa = 1.0 if f is None else Quant.per_tensor_scale(f, Quant.amax(a))
+    sb = 1.0 if f is None else Quant.per_tensor_scale(f, Quant.amax(b))
+    qa, qb = np.empty(n), np.empty(n)
+    clamped = Quant.quantize(a, 0, qa, 0, n, f, p, sa, rng)
+    clamped += Quant.quantize(b, 0, qb, 0, n, f, p, sb, rng)
+    out = np.empty((1, 1))
+    gemm(p, 1, 1, n, qa, 0, 0, 1, qb, 0, 0, 1, out=out, rng=rng)
+    return DotResult(float(out[0, 0]), clamped)
+
+
+def dot_sweep(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)), seeds: int = 200,
+              policies: Optional[List[NumericPolicy]] = None, sigma: float = 1.0,
+              fill=None) -> Dict:
+    """The dot sweep. Returns, per policy and length, the upper median of the
+    relative errors (DotSweep.java:152-153) and the mean clamps per pair.
+    `fill(n, seed)` may supply the vectors (for instance the reference's own
+    fill); by default they are N(0,1) x lognormal(0, sigma)."""
+    policies = policies or dot_sweep_policies()
+    exact_p = NumericPolicy.exact()
+    table: Dict[str, Dict[int, Dict[str, float]]] = {p.name: {} for p in policies}
+    rows = []
+    for n in lengths:
+        errs = {p.name: [] for p in policies}
+        clamps = {p.name: 0 for p in policies}
+        for seed in range(seeds):
+            if fill is not None:
+                a, b = fill(n, seed)
+            else:
+                rs = np.random.default_rng(seed * 7919 + n)
+                a, b = heavy_tailed(rs, n, sigma), heavy_tailed(rs, n, sigma)
+            ex = np.empty((1, 1))
+            gemm(exact_p, 1, 1, n, a, 0, 0, 1, b, 0, 0, 1, out=ex)
+            exact = float(ex[0, 0])
+            for p in policies:
+                r = dot_run(p, a, b, seed)
+                errs[p.name].append(abs(r.value - exact) / abs(exact))
+                clamps[p.name] += r.clamped
+                rows.append((p.name, n, seed, r.value, exact, r.clamped))
+        for p in policies:
+            e = sorted(errs[p.name])
+            table[p.name][n] = {"median_rel_error": e[len(e) // 2],
+                                "clamped_per_pair": clamps[p.name] / seeds}
+    return {"table": table, "rows": rows}
+
+
+def real_dot_policies() -> List[NumericPolicy]:
+    """The real-shape batch's 7 policies: FP32/FP16/BF16 sequential, FP16/BF16
+    pairwise, the e4m3 per-tensor cast and the bf16 cast (from
+    RealDotSweep.java:212-223)."""
+    b = NumericPolicy.builder
+    return [b("fp32 sequential").build(),
+            b("fp16 sequential").acc(Acc.FP16).build(),
+            b("bf16 sequential").acc(Acc.BF16).build(),
+            b("fp16 pairwise").acc(Acc.FP16).order(Order.PAIRWISE).build(),
+            b("bf16 pairwise").acc(Acc.BF16).order(Order.PAIRWISE).build(),
+            b("e4m3 per-tensor cast").input(Formats.E4M3).scaling(Scaling.PER_TENSOR).build(),
+            b("bf16 cast").input(Formats.BF16).build()]
+
+
+def real_dot_inputs(seed: int = 424242, windows: int = 4096, units: int = 64, ctx: int = 32,
+                    emb: int = 64, vocab: int = 96):
+    """Synthetic stand-ins for RealDotSweep's tensors (RealDotSweep.java:191-201):
+    X = windows of an N(0,1) embedding table picked by uniform tokens (64 groups
+    of 64 windows); W = Kaiming-normal rows, std sqrt(2 / fan_in)."""
+    rs = np.random.default_rng(seed)
+    table = rs.standard_normal((vocab, emb))
+    tokens = rs.integers(0, vocab, size=(windows, ctx))
+    X = table[tokens].reshape(windows, ctx * emb).copy()
+    W = rs.standard_normal((units, ctx * emb)) * np.sqrt(2.0 / (ctx * emb))
+    return X, W
+
+
+def true_median(v: np.ndarray) -> float:
+    """RealDotSweep's median: the mean of the two middle values (:255-256)."""
+    s = np.sort(v)
+    k = s.size
+    return 0.5 * (s[k // 2 - 1] + s[k // 2])
+
+
+def rms(v: np.ndarray) -> float:
+    """RealDotSweep.rms (:264-270)."""
+    s = 0.0
+    for x in v:
+        s += x * x
+    return float(np.sqrt(s / v.size))
+
+
+def policy_outputs(p: NumericPolicy, X: np.ndarray, W: np.ndarray, rng_seed: int = 7):
+    """RealDotSweep's per-policy flow (:235-254): Rng(7), per-tensor scales of
+    the whole X and W, cast X then W, every (window, unit) dot."""
+    f = p.input_format
+    rng = Rng(rng_seed)
+    qx, qw = X, W
+    clamped = 0
+    if f is not None:
+        sx = Quant.per_tensor_scale(f, Quant.amax(X))
+        sw = Quant.per_tensor_scale(f, Quant.amax(W))
+        qx, qw = np.empty_like(X), np.empty_like(W)
+        clamped += Quant.quantize(X, 0, qx, 0, X.size, f, p, sx, rng)
+        clamped += Quant.quantize(W, 0, qw, 0, W.size, f, p, sw, rng)
+    M, K = X.shape
+    N = W.shape[0]
+    C = gemm(p, M, N, K, qx, 0, K, 1, qw, 0, K, 1, rng=rng)
+    return C, clamped
+
+
+def real_dot_batch(X=None, W=None, policies=None) -> Dict[str, Dict[str, float]]:
+    """The real-shape batch: per policy, the true median relative error and the
+    RMS ratio over all windows x units (RealDotSweep.java:245-257)."""
+    if X is None:
+        X, W = real_dot_inputs()
+    policies = policies or real_dot_policies()
+    M, K = X.shape
+    N = W.shape[0]
+    exact = gemm(NumericPolicy.exact(), M, N, K, X, 0, K, 1, W, 0, K, 1).reshape(-1)
+    out = {}
+    for p in policies:
+        C, _ = policy_outputs(p, X, W)
+        got = C.reshape(-1)
+        err = got - exact
+        out[p.name] = {"median_rel_error": true_median(np.abs(err) / np.abs(exact)),
+                       "rms_error_ratio": rms(err) / rms(exact)}
+    return out
+
+
+def mx_policies() -> List[NumericPolicy]:
+    """The block-scaled study: e4m3 and e2m1 under per-tensor, MX spec and MX +1
+    scaling, FP32 sequential accumulation (DotSweep.java:71-82's scaling group)."""
+    b = NumericPolicy.builder
+    ps = []
+    for f in (Formats.E4M3, Formats.E2M1):
+        ps.append(b(f"{f.name} per-tensor").input(f).scaling(Scaling.PER_TENSOR).build())
+        ps.append(b(f"{f.name} mx32 spec").input(f).scaling(Scaling.MX_BLOCK).build())
+        ps.append(b(f"{f.name} mx32 +1").input(f).scaling(Scaling.MX_BLOCK).mx_headroom(1).build())
+    return ps
+
+
+def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0) -> Dict:
+    """The block-scaled GEMM at size^3 on device-resident tensors. Per policy:
+    median relative error (upper), RMS ratio, clamps per vector pair (clamps in
+    row i of A plus row j of W, averaged over pairs, as DotSweep.java:119-120
+    counts them) and per pair of 32-blocks."""
+    import torch
+
+    from .kernel import amax_dev, check_dev, gemm_dev, per_tensor_scale_dev, quantize_dev
+
+    dev = torch.device("cuda", device)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    A = (torch.randn(size, size, device=dev, generator=g) *
+         torch.exp(torch.randn(size, size, device=dev, generator=g))).double()
+    W = (torch.randn(size, size, device=dev, generator=g) *
+         torch.exp(torch.randn(size, size, device=dev, generator=g))).double()
+    exact = torch.empty_like(A)
+    gemm_dev(NumericPolicy.exact(), A, W, exact)
+    qa, qw, C = torch.empty_like(A), torch.empty_like(W), torch.empty_like(A)
+    scal = torch.zeros(4, dtype=torch.float64, device=dev)
+    res = {}
+    for p in (policies or mx_policies()):
+        f = p.input_format
+        cl = torch.zeros(2, dtype=torch.int64, device=dev)
+        for k, (src, dst) in enumerate(((A, qa), (W, qw))):
+            if p.scaling == Scaling.PER_TENSOR:
+                amax_dev(src, scal[k:k + 1])
+                per_tensor_scale_dev(f, scal[k:k + 1], scal[2 + k:3 + k])
+                quantize_dev(p, f, Rounding.NEAREST_EVEN, src, dst, d_scale=scal[2 + k:3 + k],
+                             d_clamped=cl[k:k + 1])
+            else:
+                quantize_dev(p, f, Rounding.NEAREST_EVEN, src, dst, d_clamped=cl[k:k + 1])
+        gemm_dev(p, qa, qw, C)
+        check_dev()
+        rel = ((C - exact).abs() / exact.abs()).flatten()
+        err_sq = float(((C - exact) ** 2).sum())
+        ex_sq = float((exact ** 2).sum())
+        ca, cw = (int(x) for x in cl.cpu())
+        per_pair = ca / size + cw / size
+        res[p.name] = {"median_rel_error": float(rel.kthvalue(rel.numel() // 2 + 1).values),
+                       "rms_error_ratio": float(np.sqrt(err_sq / ex_sq)),
+                       "clamped_per_pair": per_pair,
+                       "clamped_per_block_pair": per_pair / (size // 32)}
+    return res

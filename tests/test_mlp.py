@@ -1,0 +1,90 @@
+"""The emulated MLP training step (Pass / Trainer mirror): every cast and
+every forward, dgrad and wgrad contraction on the engine, checked bit for bit
+against the same pass run on the oracle, gradients and Rng state included."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+
+class OracleBackend:
+    """Casts and contractions on the oracle, for the checker's pass."""
+
+    name = "oracle"
+
+    def amax(self, x):
+        return O.amax(x)
+
+    def per_tensor_scale(self, f, amax):
+        return O.per_tensor_scale(f.id, amax)
+
+    def quantize(self, src, f, p, rm, scale, rng):
+        pc = _opolicy(p)
+        st = rng.state() if rng is not None else None
+        dst, clamped, st = O.quantize(pc, f.id if f is not None else -1, int(rm), src, scale, st)
+        if rng is not None:
+            rng.reseed(st)
+        return dst, clamped
+
+    def gemm(self, p, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks, bias=None, rng=None):
+        C, _ = O.gemm(_opolicy(p), M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks,
+                      bias=bias, threads=16)
+        return C
+
+
+def _opolicy(p):
+    c = p.to_c()
+    return O.OraclePolicy(*[getattr(c, f) for f, _ in c._fields_])
+
+
+def test_host_pieces_without_gpu():
+    """Net shapes, delayed-scaling history and the Adam update need no GPU."""
+    from drift_b200 import mlp
+    net = mlp.Net(11, 3, 4, 7, 5)
+    assert [t.size for t in net.tensors()] == [44, 84, 7, 49, 7, 77, 11]
+    p = [np.ones(3)]
+    g = [np.full(3, 0.5)]
+    m, v = [np.zeros(3)], [np.zeros(3)]
+    mlp.adam(p, g, m, v, 1, 0.1, True)
+    assert np.allclose(p[0], 0.9, atol=1e-6)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("policy", ["fp8-delayed-sr-grads", "fp8", "mxfp4-sr", "fp8-acc-bf16-pairwise",
+                                    "acc-fp16", "bf16"])
+def test_training_step_matches_oracle(policy):
+    import drift_b200 as d
+    from drift_b200 import mlp
+
+    if policy == "fp8-delayed-sr-grads":
+        p = (d.policies.by_name("fp8-delayed").to_builder(policy)
+             .grad_rounding(d.Rounding.STOCHASTIC).build())
+    else:
+        p = d.policies.by_name(policy)
+    kw = dict(vocab=23, ctx=5, emb=6, hidden=40, batch=12, steps=6, measure_every=3)
+    got = mlp.train(p, 3, **kw)
+    want = mlp.train(p, 3, backend=OracleBackend(), **kw)
+    assert got["rng_state"] == want["rng_state"]
+    for a, b in zip(got["grads"], want["grads"]):
+        assert (a.view(np.int64) == b.view(np.int64)).all()
+    for r1, r2 in zip(got["records"], want["records"]):
+        assert r1.loss == r2.loss and r1.cos == r2.cos and r1.clamp_g == r2.clamp_g
+
+
+@pytest.mark.gpu
+def test_training_step_full_size_first_steps():
+    """The training-step configuration at full size (vocab 96, ctx 32, emb 64,
+    hidden 2048, batch 64) under fp8 delayed scaling with stochastic gradient
+    rounding: two steps, every gradient bit-equal to the oracle's."""
+    import drift_b200 as d
+    from drift_b200 import mlp
+
+    p = (d.policies.by_name("fp8-delayed").to_builder("c4")
+         .grad_rounding(d.Rounding.STOCHASTIC).build())
+    got = mlp.train(p, 0, steps=2, measure_every=25)
+    want = mlp.train(p, 0, steps=2, measure_every=25, backend=OracleBackend())
+    assert got["rng_state"] == want["rng_state"]
+    for a, b in zip(got["grads"], want["grads"]):
+        assert (a.view(np.int64) == b.view(np.int64)).all()
+    r = got["records"][0]
+    assert 0.5 < r.cos <= 1.0 and r.clamp_x >= 0.0

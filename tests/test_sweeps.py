@@ -1,0 +1,114 @@
+"""The study drivers on the engine against the oracle, at the configurations'
+own shapes: the dot sweep (lengths 16..4096), the real-shape batch
+(4096 x 64 x 2048, every output) and the block-scaled GEMM (4096^3, sampled
+outputs)."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _op(p):
+    c = p.to_c()
+    return O.OraclePolicy(*[getattr(c, f) for f, _ in c._fields_])
+
+
+def _oracle_dot_run(p, a, b, seed):
+    rng = 0xD1F7 + seed
+    f = p.input_format
+    fid = f.id if f is not None else -1
+    sa = 1.0 if f is None else O.per_tensor_scale(fid, O.amax(a))
+    sb = 1.0 if f is None else O.per_tensor_scale(fid, O.amax(b))
+    op = _op(p)
+    qa, ca, rng = O.quantize(op, fid, int(p.input_rounding), a, sa, rng)
+    qb, cb, rng = O.quantize(op, fid, int(p.input_rounding), b, sb, rng)
+    v, _ = O.dot(qa, 0, 1, qb, 0, 1, a.size, op, rng)
+    return v, ca + cb
+
+
+def test_dot_sweep_baseline_shapes():
+    from drift_b200 import sweeps
+
+    out = sweeps.dot_sweep(seeds=12)
+    seen = 0
+    pols = {p.name: p for p in sweeps.dot_sweep_policies()}
+    for name, n, seed, value, exact, clamped in out["rows"]:
+        rs = np.random.default_rng(seed * 7919 + n)
+        a, b = sweeps.heavy_tailed(rs, n), sweeps.heavy_tailed(rs, n)
+        v, c = _oracle_dot_run(pols[name], a, b, seed)
+        assert v == value and c == clamped, (name, n, seed)
+        seen += 1
+    assert seen == 9 * 12 * 10
+    t = out["table"]
+    assert set(t["fp32 sequential"]) == {16, 32, 64, 128, 256, 512, 1024, 2048, 4096}
+
+
+def test_real_shape_batch_every_output():
+    from drift_b200 import sweeps
+
+    X, W = sweeps.real_dot_inputs()
+    M, K = X.shape
+    N = W.shape[0]
+    for p in sweeps.real_dot_policies():
+        got, clamped = sweeps.policy_outputs(p, X, W)
+        f = p.input_format
+        fid = f.id if f is not None else -1
+        qx, qw, cl = X, W, 0
+        rng = 7
+        if f is not None:
+            op = _op(p)
+            qx, c1, rng = O.quantize(op, fid, 0, X.reshape(-1), O.per_tensor_scale(fid, O.amax(X)), rng)
+            qw, c2, rng = O.quantize(op, fid, 0, W.reshape(-1), O.per_tensor_scale(fid, O.amax(W)), rng)
+            cl = c1 + c2
+        want, _ = O.gemm(_op(p), M, N, K, qx, 0, K, 1, qw, 0, K, 1, threads=16)
+        assert (got.view(np.int64) == want.view(np.int64)).all(), p.name
+        assert clamped == cl
+    stats = sweeps.real_dot_batch(X, W)
+    assert stats["fp32 sequential"]["median_rel_error"] < stats["bf16 sequential"]["median_rel_error"]
+
+
+def test_mx_gemm_sampled_outputs():
+    import torch
+
+    import drift_b200 as d
+    from drift_b200 import sweeps
+
+    S = 4096
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    A = (torch.randn(S, S, device=dev, generator=g) *
+         torch.exp(torch.randn(S, S, device=dev, generator=g))).double()
+    W = (torch.randn(S, S, device=dev, generator=g) *
+         torch.exp(torch.randn(S, S, device=dev, generator=g))).double()
+    rs = np.random.default_rng(0)
+    rows = np.sort(rs.choice(S, 8, replace=False))
+    cols = np.sort(rs.choice(S, 64, replace=False))
+    for p in sweeps.mx_policies():
+        f = p.input_format
+        qa, qw, C = torch.empty_like(A), torch.empty_like(W), torch.empty_like(A)
+        scal = torch.zeros(4, dtype=torch.float64, device=dev)
+        scales = [1.0, 1.0]
+        for k, (src, dst) in enumerate(((A, qa), (W, qw))):
+            if p.scaling == d.Scaling.PER_TENSOR:
+                d.amax_dev(src, scal[k:k + 1])
+                d.per_tensor_scale_dev(f, scal[k:k + 1], scal[2 + k:3 + k])
+                d.quantize_dev(p, f, d.Rounding.NEAREST_EVEN, src, dst, d_scale=scal[2 + k:3 + k])
+            else:
+                d.quantize_dev(p, f, d.Rounding.NEAREST_EVEN, src, dst)
+        d.gemm_dev(p, qa, qw, C)
+        d.check_dev()
+        scales = [float(x) for x in scal[2:4].cpu()]
+        a_rows = A[rows].cpu().numpy().reshape(-1)
+        w_rows = W[cols].cpu().numpy().reshape(-1)
+        op = _op(p)
+        oqa, _, _ = O.quantize(op, f.id, 0, a_rows, scales[0])
+        oqw, _, _ = O.quantize(op, f.id, 0, w_rows, scales[1])
+        assert (qa[rows].cpu().numpy().reshape(-1).view(np.int64) == oqa.view(np.int64)).all()
+        want, _ = O.gemm(op, len(rows), len(cols), S, oqa, 0, S, 1, oqw, 0, S, 1, threads=16)
+        got = C[rows][:, cols].cpu().numpy()
+        assert (got.view(np.int64) == want.view(np.int64)).all(), p.name
+    res = sweeps.mx_gemm(1024, policies=sweeps.mx_policies()[:2])
+    assert res["e4m3 mx32 spec"]["clamped_per_pair"] > 0.0
