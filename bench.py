@@ -181,6 +181,7 @@ def run_engine(args):
     import drift_b200 as d
 
     from drift_b200 import dist as ddist
+    from drift_b200 import stats as dstats
 
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
@@ -213,6 +214,8 @@ def run_engine(args):
     Cx = torch.empty((M, N), dtype=torch.float64, device=dev)
     n_pol = len(pols)
     sums = torch.zeros((n_pol, 2), dtype=torch.float64, device=dev)
+    med_state = torch.zeros((n_pol, 2), dtype=torch.int64, device=dev)
+    med_hist = torch.empty(dstats.RADIX_BINS, dtype=torch.int64, device=dev)
     clamps = torch.zeros((n_pol, 2), dtype=torch.int64, device=dev)  # clamps in A, in B
     scal = torch.zeros((4,), dtype=torch.float64, device=dev)  # amax A, amax B, scale A, scale B
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -247,7 +250,11 @@ def run_engine(args):
             d.gemm_dev(p, a, b, C, ctx=ctx)
             ev[k + 1][1].record(stream)
             d.error_sums_dev(C, Cx, sums[k], ctx=ctx)
-            launches[0] += 2
+            # DotSweep's summary statistic over every rank's outputs: the upper
+            # median of the relative errors (DotSweep.java:152-153).
+            dstats.select_rel_error_dev(C, Cx, (world * M * N) // 2, med_state[k], med_hist,
+                                        dist=pg, ctx=ctx)
+            launches[0] += 2 + 2 * dstats.RADIX_PASSES
         ddist.reduce_stats(sums, clamps, pg)
 
     def barrier():
@@ -293,7 +300,9 @@ def run_engine(args):
     # Statistics (summed over ranks): RMS ratio and clamps per pair.
     s = sums.cpu().numpy()
     c = clamps.cpu().numpy()
-    stats = {p.name: {"rms_error_ratio": ddist.rms_ratio(float(s[k, 0]), float(s[k, 1])),
+    med = med_state.cpu().numpy()
+    stats = {p.name: {"median_rel_error": dstats.bits_to_double(med[k, 0]),
+                      "rms_error_ratio": ddist.rms_ratio(float(s[k, 0]), float(s[k, 1])),
                       # DotSweep's clamps per pair (DotSweep.java:119-120): clamps in
                       # row i of A plus clamps in row j of B, averaged over all pairs.
                       "clamped_per_pair": (float(c[k, 0]) / M + float(c[k, 1]) / N)

@@ -69,6 +69,8 @@ SIGNATURES = {
     "drift_gemm_dev": (_int, [_vp, _P(DriftPolicy), _i64, _i64, _i64, _vp, _i64, _i64, _vp,
                               _i64, _i64, _vp, _vp, _i64, _vp]),
     "drift_error_sums_dev": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
+    "drift_radix_hist_dev": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp]),
+    "drift_radix_select_dev": (_int, [_vp, _int, _vp, _vp, _vp]),
     "drift_probe_fp64": (_int, [_vp, _P(_d)]),
     "drift_check_dev": (_int, [_vp, _vp]),
 }

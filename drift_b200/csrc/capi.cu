@@ -458,6 +458,27 @@ int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, 
               : DRIFT_OK;
 }
 
+int drift_radix_hist_dev(drift_ctx *ctx, const double *d_got, const double *d_exact, int64_t n,
+                         int pass, const uint64_t *d_state, uint64_t *d_hist, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || !d_state || !d_hist || (n > 0 && (!d_got || !d_exact)))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_radix_pass(d_got, d_exact, n, pass, (unsigned long long *)d_state,
+                           (unsigned long long *)d_hist, pick(ctx, stream));
+    return rc ? fail(rc, "radix histogram") : DRIFT_OK;
+}
+
+int drift_radix_select_dev(drift_ctx *ctx, int pass, const uint64_t *d_hist, uint64_t *d_state,
+                           void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!d_state || !d_hist) return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_radix_select(pass, (const unsigned long long *)d_hist,
+                             (unsigned long long *)d_state, pick(ctx, stream));
+    return rc ? fail(rc, "radix select") : DRIFT_OK;
+}
+
 int drift_probe_fp64(drift_ctx *ctx, double *ops_per_s) {
     int rc = enter(ctx);
     if (rc) return rc;

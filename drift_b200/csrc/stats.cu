@@ -55,4 +55,93 @@ int launch_error_sums(const double *got, const double *exact, int64_t n, double 
     return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 
+// ------------------------------------------------------------------ exact order statistics
+//
+// The k-th smallest relative error |got - exact| / |exact| (the median of
+// DotSweep.java:152-153 and RealDotSweep.java:255-256) over all outputs, found
+// by radix selection on the double's bit pattern: for non-negative doubles
+// the bits order like the values, and NaN (0/0) is mapped above +Inf, where
+// Java's sort puts it. Six passes of 11, 11, 11, 11, 11 and 9 bits each read
+// both outputs once, histogram the next digit of the elements that match the
+// digits chosen so far, and a one-CTA kernel picks the digit holding rank k.
+// Between the passes the histograms of several ranks can be summed (NCCL), so
+// the selection is over the union of every rank's outputs.
+
+constexpr int kRadixBits = 11;
+constexpr int kRadixBins = 1 << kRadixBits;
+constexpr int kRadixPasses = 6;
+
+__device__ __forceinline__ uint64_t rel_error_key(double got, double exact) {
+    const double rel = fabs(__dsub_rn(got, exact)) / fabs(exact);  // IEEE division
+    return isnan(rel) ? ~0ULL : dbits(rel);
+}
+
+__host__ __device__ inline int radix_shift(int pass) {
+    const int s = 64 - kRadixBits * (pass + 1);
+    return s < 0 ? 0 : s;
+}
+
+__global__ void __launch_bounds__(256) radix_hist_kernel(const double *got, const double *exact,
+                                                         int64_t n, int pass,
+                                                         const unsigned long long *state,
+                                                         unsigned long long *hist) {
+    __shared__ unsigned int s_hist[kRadixBins];
+    for (int i = threadIdx.x; i < kRadixBins; i += blockDim.x) s_hist[i] = 0;
+    __syncthreads();
+    const int shift = radix_shift(pass);
+    const int top = 64 - kRadixBits * pass;  // bits >= top are already chosen
+    const uint64_t prefix = state[0];
+    const uint64_t mask = (uint64_t)((1u << (top - shift)) - 1u);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const uint64_t key = rel_error_key(got[i], exact[i]);
+        if (top == 64 || (key >> top) == (prefix >> top))
+            atomicAdd(&s_hist[(key >> shift) & mask], 1u);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kRadixBins; i += blockDim.x)
+        if (s_hist[i]) atomicAdd(&hist[i], (unsigned long long)s_hist[i]);
+}
+
+// state[0] = digits chosen so far, state[1] = rank still sought among the
+// elements that match them. One thread scans the bins in order.
+__global__ void radix_select_kernel(int pass, const unsigned long long *hist,
+                                    unsigned long long *state) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int shift = radix_shift(pass);
+    const int width = 64 - kRadixBits * pass - shift;
+    unsigned long long k = state[1];
+    int bin = 0;
+    for (; bin < (1 << width); bin++) {
+        if (k < hist[bin]) break;
+        k -= hist[bin];
+    }
+    if (bin == (1 << width)) bin = (1 << width) - 1;  // k out of range: stay at the top
+    state[0] |= (unsigned long long)bin << shift;
+    state[1] = k;
+}
+
+int launch_radix_pass(const double *got, const double *exact, int64_t n, int pass,
+                      unsigned long long *state, unsigned long long *hist, cudaStream_t st) {
+    if (pass < 0 || pass >= kRadixPasses) return DRIFT_EINVAL;
+    if (cudaMemsetAsync(hist, 0, kRadixBins * sizeof(unsigned long long), st) != cudaSuccess)
+        return DRIFT_ECUDA;
+    if (n > 0) {
+        int sms = 148, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        int64_t blocks = (n + 255) / 256;
+        if (blocks > sms * 4) blocks = sms * 4;
+        radix_hist_kernel<<<(unsigned)blocks, 256, 0, st>>>(got, exact, n, pass, state, hist);
+    }
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+}
+
+int launch_radix_select(int pass, const unsigned long long *hist, unsigned long long *state,
+                        cudaStream_t st) {
+    if (pass < 0 || pass >= kRadixPasses) return DRIFT_EINVAL;
+    radix_select_kernel<<<1, 32, 0, st>>>(pass, hist, state);
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+}
+
 }  // namespace drift

@@ -264,6 +264,29 @@ DRIFT_API int drift_error_sums_dev(drift_ctx *ctx, const double *d_got,
                                    const double *d_exact, int64_t n,
                                    double *d_sums, void *stream);
 
+/*
+ * Exact order statistics of the relative error |got - exact| / |exact| over
+ * all n outputs (the medians of java/.../tools/DotSweep.java:152-153 and
+ * RealDotSweep.java:255-256), by radix selection on the double's bits in
+ * DRIFT_RADIX_PASSES passes. d_state holds two uint64: the digits chosen so
+ * far (start at 0) and the 0-based rank sought (start at k). Each pass:
+ * drift_radix_hist_dev clears d_hist (DRIFT_RADIX_BINS uint64) and counts the
+ * next digit of the elements still in play; several ranks may then sum their
+ * d_hist (all-reduce) so the selection runs over all of their outputs; then
+ * drift_radix_select_dev picks the digit. After the last pass d_state[0] is
+ * the bit pattern of the k-th smallest relative error (NaN, from 0/0, sorts
+ * after +Inf as Java's sort places it).
+ */
+#define DRIFT_RADIX_PASSES 6
+#define DRIFT_RADIX_BINS 2048
+DRIFT_API int drift_radix_hist_dev(drift_ctx *ctx, const double *d_got,
+                                   const double *d_exact, int64_t n, int pass,
+                                   const uint64_t *d_state, uint64_t *d_hist,
+                                   void *stream);
+DRIFT_API int drift_radix_select_dev(drift_ctx *ctx, int pass,
+                                     const uint64_t *d_hist, uint64_t *d_state,
+                                     void *stream);
+
 /* ----------------------------------------------------------- diagnostics */
 /* No counterpart in the reference: measures the FP64 pipe's DMUL+DADD issue
  * rate on the context's device (operations per second), the denominator of
