@@ -78,37 +78,37 @@ struct GemmArgs {
 // doubles, and a miss recomputes those eight exactly.
 constexpr int GROUP_ROWS = 2;
 
-// Rounds sixteen sums as the accumulator does (Dot.java:54, :63, :99, :224).
+// Rounds sixteen sums in place as the accumulator does (Dot.java:54, :63,
+// :99, :224). The rounded value overwrites the sum and the sum is kept aside
+// only until its group is validated, so no copy is needed on the fast path.
 template <int ACC, int RM>
 __device__ __forceinline__ void round16(double (&t)[TM][TN]) {
     using R = AccRound<ACC, RM>;
     if constexpr (ACC != DRIFT_ACC_FP64) {
 #pragma unroll
-    for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
-        double r[GROUP_ROWS][TN];
-        bool ok = true;
-#pragma unroll
-        for (int i = 0; i < GROUP_ROWS; i++)
-#pragma unroll
-            for (int j = 0; j < TN; j++) {
-                r[i][j] = R::fast(t[i0 + i][j]);
-                ok = ok & R::ok(r[i][j]);
-            }
-        if (!ok) {
+        for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
+            double keep[GROUP_ROWS][TN];
+            bool ok = true;
 #pragma unroll
             for (int i = 0; i < GROUP_ROWS; i++)
 #pragma unroll
-                for (int j = 0; j < TN; j++) r[i][j] = R::exact(t[i0 + i][j]);
+                for (int j = 0; j < TN; j++) {
+                    keep[i][j] = t[i0 + i][j];
+                    t[i0 + i][j] = R::fast(keep[i][j]);
+                    ok = ok & R::ok(t[i0 + i][j]);
+                }
+            if (!ok) {
+#pragma unroll
+                for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+                    for (int j = 0; j < TN; j++) t[i0 + i][j] = R::exact(keep[i][j]);
+            }
         }
-#pragma unroll
-        for (int i = 0; i < GROUP_ROWS; i++)
-#pragma unroll
-            for (int j = 0; j < TN; j++) t[i0 + i][j] = r[i][j];
-    }
     }
 }
 
-// One k step for the thread's 16 outputs: acc = round(acc + a_i * b_j).
+// One k step for the thread's 16 outputs: acc = round(acc + a_i * b_j), the
+// rounded value written straight into the accumulator.
 template <int ACC, int RM>
 __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[TM],
                                       const double (&b)[TN]) {
@@ -121,26 +121,22 @@ __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[T
     } else {
 #pragma unroll
         for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
-            double r[GROUP_ROWS][TN];
+            double t[GROUP_ROWS][TN];
             bool ok = true;
 #pragma unroll
             for (int i = 0; i < GROUP_ROWS; i++)
 #pragma unroll
                 for (int j = 0; j < TN; j++) {
-                    r[i][j] = R::fast(__dadd_rn(acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j])));
-                    ok = ok & R::ok(r[i][j]);
+                    t[i][j] = __dadd_rn(acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j]));
+                    acc[i0 + i][j] = R::fast(t[i][j]);
+                    ok = ok & R::ok(acc[i0 + i][j]);
                 }
-            if (!ok) {  // rare: recompute these eight exactly from the same operands
+            if (!ok) {  // rare: round these eight sums exactly
 #pragma unroll
                 for (int i = 0; i < GROUP_ROWS; i++)
 #pragma unroll
-                    for (int j = 0; j < TN; j++)
-                        r[i][j] = R::exact(__dadd_rn(acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j])));
+                    for (int j = 0; j < TN; j++) acc[i0 + i][j] = R::exact(t[i][j]);
             }
-#pragma unroll
-            for (int i = 0; i < GROUP_ROWS; i++)
-#pragma unroll
-                for (int j = 0; j < TN; j++) acc[i0 + i][j] = r[i][j];
         }
     }
 }
