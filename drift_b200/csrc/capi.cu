@@ -395,7 +395,7 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
     if (sb) CUDA_TRY(cudaMemcpyAsync(d_b, B + b_off, sb * 8, cudaMemcpyHostToDevice, st), "copy B");
     if (bias) CUDA_TRY(cudaMemcpyAsync(d_bias, bias, N * 8, cudaMemcpyHostToDevice, st), "copy bias");
     rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
-                     b_row_stride, b_k_stride, d_bias, d_c, N, st);
+                     b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), st);
     if (rc) return fail(rc, rc == DRIFT_EUNSUPPORTED ? "stochastic accumulator rounding is not supported"
                                                      : "gemm launch");
     CUDA_TRY(cudaMemcpy2DAsync(C, c_row_stride * 8, d_c, N * 8, N * 8, M, cudaMemcpyDeviceToHost, st),
@@ -452,7 +452,8 @@ int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, 
     if (!p || c_row_stride < N) return fail(DRIFT_EINVAL, "bad shape or stride");
     if (M > 0 && N > 0 && (!d_C || (K > 0 && (!d_A || !d_B)))) return fail(DRIFT_EINVAL, "null buffer");
     rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
-                     b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, pick(ctx, stream));
+                     b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->d_err(),
+                     pick(ctx, stream));
     return rc ? fail(rc, rc == DRIFT_EUNSUPPORTED ? "stochastic accumulator rounding is not supported"
                                                   : "gemm launch")
               : DRIFT_OK;

@@ -69,6 +69,6 @@ int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
-                cudaStream_t st);
+                int *d_err, cudaStream_t st);
 
 }  // namespace drift
