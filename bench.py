@@ -36,6 +36,12 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 METRIC = "bit-exact emulated MAC/s per policy at 1/2/4/8 B200 vs Java host; mismatches=0"
+
+# DRAM bytes per emulated MAC of the contraction, from one ncu capture of the
+# same kernels at 4096^3 (dram__bytes_read.sum + dram__bytes_write.sum per
+# launch over its MACs); a launch's traffic scales with its MAC count because
+# every operand tile is re-read once per 64-wide output tile.
+DRAM_BYTES_PER_MAC = {"pairwise": 0.159, "other": 0.0566}
 UNIT = "emulated MAC/s"
 
 
@@ -293,6 +299,10 @@ def run_engine(args):
     fp64_peak = d.probe_fp64(ctx)
     gemm_total_ms = sum(gemm_ms)
     achieved = 2.0 * macs_per_step_rank / (gemm_total_ms * 1e-3)
+    n_pair = sum(1 for p in pols if p.order == d.Order.PAIRWISE)
+    traffic_per_launch = M * N * K * (n_pair * DRAM_BYTES_PER_MAC["pairwise"] +
+                                      (len(pols) + 1 - n_pair) * DRAM_BYTES_PER_MAC["other"]) \
+        / (len(pols) + 1)
     per_policy = {"exact fp64": M * N * K / (gemm_ms[0] * 1e-3)}
     for k, p in enumerate(pols):
         per_policy[p.name] = M * N * K / (gemm_ms[k + 1] * 1e-3)
@@ -332,7 +342,9 @@ def run_engine(args):
                    "l2": "inputs (2 x 512 MiB at 8192) are larger than L2",
                    "parallelism": f"shard by seed x{world}"},
         "roofline": {"bound": "fp64", "achieved": achieved / 1e12, "peak": fp64_peak / 1e12,
-                     "unit": "TFLOP/s", "frac": achieved / fp64_peak, "traffic": None,
+                     "unit": "TFLOP/s", "frac": achieved / fp64_peak,
+                     "traffic": traffic_per_launch,
+                     "traffic_unit": "bytes per contraction launch, averaged over the step's 13",
                      "kernel": "gemm_kernel (all policies)",
                      "peak_source": "measured DMUL+DADD probe (drift_probe_fp64) on this GPU"},
         "per_policy_mac_per_s": per_policy,
