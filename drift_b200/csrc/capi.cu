@@ -368,11 +368,15 @@ static int64_t span_of(int64_t rows, int64_t rs, int64_t K, int64_t ks) {
     return (rows - 1) * rs + (K - 1) * ks + 1;
 }
 
+static bool stochastic_acc(const drift_policy *p) {
+    return (p->acc == DRIFT_ACC_FP16 || p->acc == DRIFT_ACC_BF16) &&
+           p->acc_rounding == DRIFT_STOCHASTIC;
+}
+
 int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int64_t K,
                const double *A, int64_t a_off, int64_t a_row_stride, int64_t a_k_stride,
                const double *B, int64_t b_off, int64_t b_row_stride, int64_t b_k_stride,
                const double *bias, double *C, int64_t c_row_stride, uint64_t *rng_state) {
-    (void)rng_state;  // no accumulator this engine supports draws random numbers
     int rc = enter(ctx);
     if (rc) return rc;
     if (!p || M < 0 || N < 0 || K < 0 || a_off < 0 || b_off < 0 || a_row_stride < 0 ||
@@ -394,13 +398,29 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
     if (sa) CUDA_TRY(cudaMemcpyAsync(d_a, A + a_off, sa * 8, cudaMemcpyHostToDevice, st), "copy A");
     if (sb) CUDA_TRY(cudaMemcpyAsync(d_b, B + b_off, sb * 8, cudaMemcpyHostToDevice, st), "copy B");
     if (bias) CUDA_TRY(cudaMemcpyAsync(d_bias, bias, N * 8, cudaMemcpyHostToDevice, st), "copy bias");
-    rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
-                     b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), st);
-    if (rc) return fail(rc, rc == DRIFT_EUNSUPPORTED ? "stochastic accumulator rounding is not supported"
-                                                     : "gemm launch");
+    const bool sr = stochastic_acc(p);
+    if (sr) {
+        // The Rng state travels on the device; without one, start from zero
+        // and fail afterwards if any draw was taken (Java fails on the first).
+        const uint64_t s0 = rng_state ? *rng_state : 0;
+        CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), &s0, 8, cudaMemcpyHostToDevice, st), "rng in");
+        rc = launch_gemm_sr(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
+                            b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_state(), st);
+    } else {
+        rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
+                         b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), st);
+    }
+    if (rc) return fail(rc, "gemm launch");
     CUDA_TRY(cudaMemcpy2DAsync(C, c_row_stride * 8, d_c, N * 8, N * 8, M, cudaMemcpyDeviceToHost, st),
              "copy C");
-    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    uint64_t s1 = 0;
+    if (sr) CUDA_TRY(cudaMemcpyAsync(&s1, ctx->d_state(), 8, cudaMemcpyDeviceToHost, st), "rng out");
+    rc = take_device_error(ctx, st);
+    if (rc) return rc;
+    if (sr) {
+        if (!rng_state && s1 != 0) return fail(DRIFT_EINVAL, "stochastic rounding needs an Rng");
+        if (rng_state) *rng_state = s1;
+    }
     return DRIFT_OK;
 }
 
@@ -446,17 +466,22 @@ int drift_error_sums_dev(drift_ctx *ctx, const double *d_got, const double *d_ex
 int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int64_t K,
                    const double *d_A, int64_t a_row_stride, int64_t a_k_stride, const double *d_B,
                    int64_t b_row_stride, int64_t b_k_stride, const double *d_bias, double *d_C,
-                   int64_t c_row_stride, void *stream) {
+                   int64_t c_row_stride, uint64_t *d_rng_state, void *stream) {
     int rc = enter(ctx);
     if (rc) return rc;
-    if (!p || c_row_stride < N) return fail(DRIFT_EINVAL, "bad shape or stride");
+    if (!p || c_row_stride < N || M < 0 || N < 0 || K < 0) return fail(DRIFT_EINVAL, "bad shape or stride");
     if (M > 0 && N > 0 && (!d_C || (K > 0 && (!d_A || !d_B)))) return fail(DRIFT_EINVAL, "null buffer");
-    rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
-                     b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->d_err(),
-                     pick(ctx, stream));
-    return rc ? fail(rc, rc == DRIFT_EUNSUPPORTED ? "stochastic accumulator rounding is not supported"
-                                                  : "gemm launch")
-              : DRIFT_OK;
+    if (stochastic_acc(p)) {
+        if (!d_rng_state) return fail(DRIFT_EINVAL, "stochastic accumulation needs d_rng_state");
+        rc = launch_gemm_sr(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
+                            b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, d_rng_state,
+                            pick(ctx, stream));
+    } else {
+        rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
+                         b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->d_err(),
+                         pick(ctx, stream));
+    }
+    return rc ? fail(rc, "gemm launch") : DRIFT_OK;
 }
 
 int drift_radix_hist_dev(drift_ctx *ctx, const double *d_got, const double *d_exact, int64_t n,

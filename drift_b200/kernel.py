@@ -281,9 +281,12 @@ def _tptr(t) -> int:
 
 
 def gemm_dev(p: NumericPolicy, A, B, C, *, M=None, N=None, K=None, a_rs=None, a_ks=1,
-             b_rs=None, b_ks=1, c_rs=None, bias=None, stream=None, ctx=None) -> None:
+             b_rs=None, b_ks=1, c_rs=None, bias=None, d_rng_state=None, stream=None,
+             ctx=None) -> None:
     """The contraction on device tensors. Defaults describe the forward layout:
-    A is M x K and B is N x K, both K-contiguous; C is M x N."""
+    A is M x K and B is N x K, both K-contiguous; C is M x N. A stochastic
+    accumulator needs d_rng_state (an int64 device tensor of one element
+    holding the Rng state's bits), which it advances."""
     M = A.shape[0] if M is None else M
     K = A.shape[1] if K is None else K
     N = B.shape[0] if N is None else N
@@ -294,7 +297,7 @@ def gemm_dev(p: NumericPolicy, A, B, C, *, M=None, N=None, K=None, a_rs=None, a_
     pc = p.to_c()
     _lib.check(_lib.load().drift_gemm_dev(ctx.handle, ctypes.byref(pc), M, N, K, _tptr(A), a_rs,
                                           a_ks, _tptr(B), b_rs, b_ks, _tptr(bias), _tptr(C), c_rs,
-                                          _stream_ptr(stream)))
+                                          _tptr(d_rng_state), _stream_ptr(stream)))
 
 
 def quantize_dev(p: NumericPolicy, f: Optional[MiniFloat], rm: Rounding, src, dst, *,

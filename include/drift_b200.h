@@ -181,8 +181,10 @@ DRIFT_API int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt,
  * :228-232 (wgrad, both strided), java/.../tools/DotSweep.java:121 (M=N=1)
  * and java/.../tools/RealDotSweep.java:247-254. Dot.dot itself is
  * java/.../kernel/Dot.java:26-121. Strides may be any non-negative values.
- * The accumulator rounding may not be STOCHASTIC (DRIFT_EUNSUPPORTED): its
- * random stream is consumed in output order across dots.
+ * With a STOCHASTIC accumulator the dots draw from *rng_state in (i, o) order
+ * and in each dot's evaluation order, only for inexact sums, exactly as the
+ * Java loop does; on return *rng_state is advanced past every draw. A NULL
+ * rng_state is DRIFT_EINVAL only if some draw was needed.
  */
 DRIFT_API int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N,
                int64_t K, const double *A, int64_t a_off, int64_t a_row_stride,
@@ -249,13 +251,16 @@ DRIFT_API int drift_quantize_dev_noalloc(const drift_policy *p, int fmt,
                                          int64_t *d_clamped, int *d_err,
                                          void *stream);
 
-/* As drift_gemm on device buffers (offsets folded into the pointers). */
+/* As drift_gemm on device buffers (offsets folded into the pointers). With a
+ * STOCHASTIC accumulator the Rng state is the device uint64 *d_rng_state
+ * (required then, ignored otherwise), advanced on the device; that case
+ * synchronises the stream once per settling pass. */
 DRIFT_API int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
                    int64_t N, int64_t K, const double *d_A,
                    int64_t a_row_stride, int64_t a_k_stride, const double *d_B,
                    int64_t b_row_stride, int64_t b_k_stride,
                    const double *d_bias, double *d_C, int64_t c_row_stride,
-                   void *stream);
+                   uint64_t *d_rng_state, void *stream);
 
 /* Error sums of RealDotSweep's RMS ratio
  * (java/.../tools/RealDotSweep.java:245-257): ADDS sum((got-exact)^2) to

@@ -139,13 +139,6 @@ def test_every_order_agrees_in_fp64(d):
         assert abs(d.Dot.dot(a, 0, 1, b, 0, 1, 1000, p) - plain) <= 1e-12 * abs(plain)
 
 
-def test_stochastic_accumulator_is_reported_unsupported(d):
-    p = d.policies.by_name("fp8-acc-bf16-sr")
-    with pytest.raises(d.DriftError) as e:
-        d.Dot.dot(np.ones(4), 0, 1, np.ones(4), 0, 1, 4, p, d.Rng(1))
-    assert e.value.status == 5
-
-
 def test_large_fp32_sampled_outputs(d):
     """A 1024 x 1024 x 2048 product: every sampled output equals the oracle."""
     import torch

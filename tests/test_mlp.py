@@ -27,8 +27,11 @@ class OracleBackend:
         return dst, clamped
 
     def gemm(self, p, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks, bias=None, rng=None):
-        C, _ = O.gemm(_opolicy(p), M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks,
-                      bias=bias, threads=16)
+        st = rng.state() if rng is not None else None
+        C, st = O.gemm(_opolicy(p), M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks,
+                       bias=bias, rng_state=st, threads=16)
+        if rng is not None:
+            rng.reseed(st)
         return C
 
 
@@ -51,7 +54,7 @@ def test_host_pieces_without_gpu():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("policy", ["fp8-delayed-sr-grads", "fp8", "mxfp4-sr", "fp8-acc-bf16-pairwise",
-                                    "acc-fp16", "bf16"])
+                                    "acc-fp16", "bf16", "fp8-acc-bf16-sr"])
 def test_training_step_matches_oracle(policy):
     import drift_b200 as d
     from drift_b200 import mlp
