@@ -53,6 +53,11 @@ SIGNATURES = {
     "drift_format_info": (_int, [_int, _P(_d), _P(_d), _P(_d), _P(_i32)]),
     "drift_encode": (_int, [_vp, _int, _int, _vp, _vp, _i64, _P(ctypes.c_uint64)]),
     "drift_decode": (_int, [_vp, _int, _vp, _vp, _i64]),
+    "drift_value_table": (_int, [_vp, _int, _vp]),
+    "drift_pair_table": (_int, [_vp, _int, _int, ctypes.c_uint64, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "drift_value_table_dev": (_int, [_vp, _int, _vp, _vp]),
+    "drift_pair_table_dev": (_int, [_vp, _int, _int, ctypes.c_uint64, _i64, _i64, _vp, _vp, _vp,
+                                    _vp, _vp]),
     "drift_acc_round": (_int, [_vp, _int, _int, _vp, _vp, _i64, _P(ctypes.c_uint64)]),
     "drift_amax": (_int, [_vp, _vp, _i64, _P(_d)]),
     "drift_per_tensor_scale": (_int, [_int, _d, _P(_d)]),

@@ -284,6 +284,62 @@ int drift_decode(drift_ctx *ctx, int fmt, const int32_t *codes, double *v, int64
     return DRIFT_OK;
 }
 
+int drift_value_table_dev(drift_ctx *ctx, int fmt, uint64_t *d_bits, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!d_bits) return fail(DRIFT_EINVAL, "null pointer");
+    rc = launch_value_table(fmt, d_bits, pick(ctx, stream));
+    return rc ? fail(rc, "value table") : DRIFT_OK;
+}
+
+int drift_pair_table_dev(drift_ctx *ctx, int fmt, int mode, uint64_t seed, int64_t first,
+                         int64_t n, int32_t *d_a, int32_t *d_b, int32_t *d_prod, int32_t *d_sum,
+                         void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n > 0 && (!d_prod || !d_sum)) return fail(DRIFT_EINVAL, "null pointer");
+    rc = launch_pair_table(fmt, mode, seed, first, n, d_a, d_b, d_prod, d_sum, pick(ctx, stream));
+    return rc ? fail(rc, "pair table") : DRIFT_OK;
+}
+
+int drift_value_table(drift_ctx *ctx, int fmt, uint64_t *bits) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    FmtDesc f;
+    if (!fmt_desc(fmt, &f)) return fail(DRIFT_EINVAL, "bad format id");
+    if (!bits) return fail(DRIFT_EINVAL, "null pointer");
+    const int64_t codes = (int64_t)f.code_mask + 1;
+    cudaStream_t st = ctx->stream;
+    uint64_t *d_bits = (uint64_t *)ctx->io.get((size_t)codes * 8, st);
+    if (!d_bits) return fail(DRIFT_ENOMEM, "staging");
+    rc = launch_value_table(fmt, d_bits, st);
+    if (rc) return fail(rc, "value table");
+    CUDA_TRY(cudaMemcpyAsync(bits, d_bits, codes * 8, cudaMemcpyDeviceToHost, st), "copy out");
+    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    return DRIFT_OK;
+}
+
+int drift_pair_table(drift_ctx *ctx, int fmt, int mode, uint64_t seed, int64_t first, int64_t n,
+                     int32_t *a, int32_t *b, int32_t *prod, int32_t *sum) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || (n > 0 && (!prod || !sum))) return fail(DRIFT_EINVAL, "bad arguments");
+    if (n == 0) return launch_pair_table(fmt, mode, seed, first, 0, 0, 0, 0, 0, ctx->stream)
+                          ? fail(DRIFT_EINVAL, "bad arguments") : DRIFT_OK;
+    cudaStream_t st = ctx->stream;
+    int32_t *buf = (int32_t *)ctx->io.get((size_t)n * 16, st);
+    if (!buf) return fail(DRIFT_ENOMEM, "staging");
+    rc = launch_pair_table(fmt, mode, seed, first, n, buf, buf + n, buf + 2 * n, buf + 3 * n, st);
+    if (rc) return fail(rc, "pair table");
+    int32_t *outs[4] = {a, b, prod, sum};
+    for (int j = 0; j < 4; j++)
+        if (outs[j])
+            CUDA_TRY(cudaMemcpyAsync(outs[j], buf + j * n, n * 4, cudaMemcpyDeviceToHost, st),
+                     "copy out");
+    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    return DRIFT_OK;
+}
+
 int drift_acc_round(drift_ctx *ctx, int acc, int rounding, const double *x, double *y, int64_t n,
                     uint64_t *rng_state) {
     int rc = enter(ctx);

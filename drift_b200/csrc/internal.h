@@ -75,4 +75,9 @@ int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int6
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
                 int *d_err, cudaStream_t st);
 
+// tables.cu
+int launch_value_table(int fmt, uint64_t *d_bits, cudaStream_t st);
+int launch_pair_table(int fmt, int mode, uint64_t seed, int64_t first, int64_t n, int32_t *d_a,
+                      int32_t *d_b, int32_t *d_prod, int32_t *d_sum, cudaStream_t st);
+
 }  // namespace drift

@@ -148,6 +148,27 @@ DRIFT_API int drift_encode(drift_ctx *ctx, int fmt, int rounding, const double *
 DRIFT_API int drift_decode(drift_ctx *ctx, int fmt, const int32_t *codes, double *v,
                  int64_t n);
 
+/*
+ * DumpTables (java/.../tools/DumpTables.java:61-124) from the device codec.
+ * drift_value_table: the raw double bits of decode(c) for every code c of the
+ * format, `bits` holding 2^width entries (values_<fmt>.csv, :61-79).
+ * drift_pair_table: rows first .. first+n-1 of pairs_<fmt>.csv, the
+ * nearest-even code of the exact product and of the exact sum of a code
+ * pair. DRIFT_PAIRS_EXHAUSTIVE: row p is (p / codes, p % codes), p < codes^2
+ * (:87-100). DRIFT_PAIRS_SAMPLED: row p uses the Rng draws 2p and 2p+1 of a
+ * stream seeded `seed`, each taken as (nextLong() >>> 1) % codes
+ * (:106-124; DumpTables seeds 0x51ED1EA5). `a` and `b` may be NULL.
+ */
+#define DRIFT_PAIRS_EXHAUSTIVE 0
+#define DRIFT_PAIRS_SAMPLED    1
+DRIFT_API int drift_value_table(drift_ctx *ctx, int fmt, uint64_t *bits);
+DRIFT_API int drift_pair_table(drift_ctx *ctx, int fmt, int mode, uint64_t seed, int64_t first,
+                     int64_t n, int32_t *a, int32_t *b, int32_t *prod, int32_t *sum);
+DRIFT_API int drift_value_table_dev(drift_ctx *ctx, int fmt, uint64_t *d_bits, void *stream);
+DRIFT_API int drift_pair_table_dev(drift_ctx *ctx, int fmt, int mode, uint64_t seed,
+                         int64_t first, int64_t n, int32_t *d_a, int32_t *d_b,
+                         int32_t *d_prod, int32_t *d_sum, void *stream);
+
 /* Dot.round(x, acc, rm, rng) over an array, element order
  * (java/.../kernel/Dot.java:141-182). acc is DRIFT_ACC_FP16 or _BF16. */
 DRIFT_API int drift_acc_round(drift_ctx *ctx, int acc, int rounding, const double *x,
