@@ -41,6 +41,16 @@ class DriftPolicy(ctypes.Structure):
         "acc_rounding", "master_fp32", "cast_scores", "cast_probs", "reserved")]
 
 
+class DriftContraction(ctypes.Structure):
+    """struct drift_contraction (include/drift_b200.h)."""
+
+    _fields_ = [(n, ctypes.c_int64) for n in (
+        "batch", "rows", "cols", "depth", "a_off", "a_batch", "a_row", "a_k", "b_off", "b_batch",
+        "b_col", "b_k", "c_off", "c_batch", "c_row", "c_col")] + [
+        ("alpha", ctypes.c_double), ("window", ctypes.c_int32), ("causal", ctypes.c_int32),
+        ("accumulate", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
 # Every exported symbol with its ctypes signature, in header order.
 _P = ctypes.POINTER
 _vp, _i32, _i64, _d = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_double
@@ -65,6 +75,10 @@ SIGNATURES = {
                               _P(ctypes.c_uint64), _P(_i64)]),
     "drift_gemm": (_int, [_vp, _P(DriftPolicy), _i64, _i64, _i64, _vp, _i64, _i64, _i64, _vp,
                           _i64, _i64, _i64, _vp, _vp, _i64, _P(ctypes.c_uint64)]),
+    "drift_contract": (_int, [_vp, _P(DriftPolicy), _P(DriftContraction), _vp, _i64, _vp, _i64,
+                              _vp, _i64, _P(ctypes.c_uint64)]),
+    "drift_contract_dev": (_int, [_vp, _P(DriftPolicy), _P(DriftContraction), _vp, _vp, _vp, _vp,
+                                  _vp]),
     "drift_amax_dev": (_int, [_vp, _vp, _i64, _vp, _vp]),
     "drift_quantize_dev": (_int, [_vp, _P(DriftPolicy), _int, _int, _vp, _vp, _i64, _vp, _d,
                                   _vp, _vp, _vp]),

@@ -429,6 +429,31 @@ static bool stochastic_acc(const drift_policy *p) {
            p->acc_rounding == DRIFT_STOCHASTIC;
 }
 
+// drift_gemm's C[i*c_rs + o] = dot(A row i, B row o) + bias[o] as a
+// one-batch contraction over the full depth.
+static ContractDesc gemm_as_contraction(int64_t M, int64_t N, int64_t K, const double *A,
+                                        int64_t a_rs, int64_t a_ks, const double *B, int64_t b_rs,
+                                        int64_t b_ks, const double *bias, double *C, int64_t c_rs) {
+    ContractDesc d{};
+    d.op.batch = 1;
+    d.op.rows = M;
+    d.op.cols = N;
+    d.op.depth = K;
+    d.op.a_row = a_rs;
+    d.op.a_k = a_ks;
+    d.op.b_col = b_rs;
+    d.op.b_k = b_ks;
+    d.op.c_row = c_rs;
+    d.op.c_col = 1;
+    d.op.alpha = 1.0;
+    d.op.window = DRIFT_WINDOW_FULL;
+    d.a = A;
+    d.b = B;
+    d.c = C;
+    d.bias = bias;
+    return d;
+}
+
 int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int64_t K,
                const double *A, int64_t a_off, int64_t a_row_stride, int64_t a_k_stride,
                const double *B, int64_t b_off, int64_t b_row_stride, int64_t b_k_stride,
@@ -460,8 +485,10 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
         // and fail afterwards if any draw was taken (Java fails on the first).
         const uint64_t s0 = rng_state ? *rng_state : 0;
         CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), &s0, 8, cudaMemcpyHostToDevice, st), "rng in");
-        rc = launch_gemm_sr(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
-                            b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_state(), st);
+        rc = launch_contract(ctx->ws, p,
+                             gemm_as_contraction(M, N, K, d_a, a_row_stride, a_k_stride, d_b,
+                                                 b_row_stride, b_k_stride, d_bias, d_c, N),
+                             ctx->d_state(), st);
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
                          b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), st);
@@ -529,15 +556,111 @@ int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, 
     if (M > 0 && N > 0 && (!d_C || (K > 0 && (!d_A || !d_B)))) return fail(DRIFT_EINVAL, "null buffer");
     if (stochastic_acc(p)) {
         if (!d_rng_state) return fail(DRIFT_EINVAL, "stochastic accumulation needs d_rng_state");
-        rc = launch_gemm_sr(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
-                            b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, d_rng_state,
-                            pick(ctx, stream));
+        rc = launch_contract(ctx->ws, p,
+                             gemm_as_contraction(M, N, K, d_A, a_row_stride, a_k_stride, d_B,
+                                                 b_row_stride, b_k_stride, d_bias, d_C,
+                                                 c_row_stride),
+                             d_rng_state, pick(ctx, stream));
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
                          b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->d_err(),
                          pick(ctx, stream));
     }
     return rc ? fail(rc, "gemm launch") : DRIFT_OK;
+}
+
+// Lowest and highest element index an affine access off + sum(coef_j * x_j),
+// 0 <= x_j < ext_j, reaches over the box of its indices.
+static void reach(int64_t off, const int64_t *coef, const int64_t *ext, int n, int64_t *lo,
+                  int64_t *hi) {
+    *lo = *hi = off;
+    for (int j = 0; j < n; j++) {
+        const int64_t span = coef[j] * (ext[j] - 1);
+        if (span > 0) *hi += span;
+        else *lo += span;
+    }
+}
+
+// Whether every element the contraction reaches lies in [0, len) of each
+// buffer. The box over (t, i, o, k) holds every window, so this is exact for
+// FULL windows and conservative for the others.
+static bool contraction_fits(const drift_contraction &op, int64_t a_len, int64_t b_len,
+                             int64_t c_len) {
+    const int64_t total = op.batch * op.rows * op.cols;
+    if (total == 0) return true;
+    int64_t lo, hi;
+    const int64_t c_coef[3] = {op.c_batch, op.c_row, op.c_col};
+    const int64_t c_ext[3] = {op.batch, op.rows, op.cols};
+    reach(op.c_off, c_coef, c_ext, 3, &lo, &hi);
+    if (lo < 0 || hi >= c_len) return false;
+    if (op.depth == 0) return true;
+    const int64_t a_coef[3] = {op.a_batch, op.a_row, op.a_k};
+    const int64_t a_ext[3] = {op.batch, op.rows, op.depth};
+    reach(op.a_off, a_coef, a_ext, 3, &lo, &hi);
+    if (lo < 0 || hi >= a_len) return false;
+    const int64_t b_coef[3] = {op.b_batch, op.b_col, op.b_k};
+    const int64_t b_ext[3] = {op.batch, op.cols, op.depth};
+    reach(op.b_off, b_coef, b_ext, 3, &lo, &hi);
+    return lo >= 0 && hi < b_len;
+}
+
+int drift_contract(drift_ctx *ctx, const drift_policy *p, const drift_contraction *op,
+                   const double *a, int64_t a_len, const double *b, int64_t b_len, double *c,
+                   int64_t c_len, uint64_t *rng_state) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || !op) return fail(DRIFT_EINVAL, "null argument");
+    rc = check_contraction(*op);
+    if (rc) return fail(rc, "bad contraction");
+    if (a_len < 0 || b_len < 0 || c_len < 0 || !contraction_fits(*op, a_len, b_len, c_len))
+        return fail(DRIFT_EINVAL, "contraction reaches outside its buffers");
+    if (op->batch * op->rows * op->cols == 0) return DRIFT_OK;
+    if (!c || (op->depth > 0 && (!a || !b))) return fail(DRIFT_EINVAL, "null buffer");
+    cudaStream_t st = ctx->stream;
+    const int64_t la = op->depth > 0 ? a_len : 0, lb = op->depth > 0 ? b_len : 0;
+    char *buf = (char *)ctx->io.get((size_t)(la + lb + c_len + 6) * 8 + 512, st);
+    if (!buf) return fail(DRIFT_ENOMEM, "staging");
+    double *d_a = (double *)buf;
+    double *d_b = d_a + ((la + 1) & ~1LL);
+    double *d_c = d_b + ((lb + 1) & ~1LL);
+    if (la) CUDA_TRY(cudaMemcpyAsync(d_a, a, la * 8, cudaMemcpyHostToDevice, st), "copy A");
+    if (lb) CUDA_TRY(cudaMemcpyAsync(d_b, b, lb * 8, cudaMemcpyHostToDevice, st), "copy B");
+    CUDA_TRY(cudaMemcpyAsync(d_c, c, c_len * 8, cudaMemcpyHostToDevice, st), "copy C");
+    const bool sr = stochastic_acc(p);
+    if (sr) {
+        const uint64_t s0 = rng_state ? *rng_state : 0;
+        CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), &s0, 8, cudaMemcpyHostToDevice, st), "rng in");
+    }
+    ContractDesc d{*op, d_a, d_b, d_c, nullptr};
+    rc = launch_contract(ctx->ws, p, d, sr ? ctx->d_state() : nullptr, st);
+    if (rc) return fail(rc, "contraction launch");
+    CUDA_TRY(cudaMemcpyAsync(c, d_c, c_len * 8, cudaMemcpyDeviceToHost, st), "copy C");
+    uint64_t s1 = 0;
+    if (sr) CUDA_TRY(cudaMemcpyAsync(&s1, ctx->d_state(), 8, cudaMemcpyDeviceToHost, st), "rng out");
+    rc = take_device_error(ctx, st);
+    if (rc) return rc;
+    if (sr) {
+        if (!rng_state && s1 != 0) return fail(DRIFT_EINVAL, "stochastic rounding needs an Rng");
+        if (rng_state) *rng_state = s1;
+    }
+    return DRIFT_OK;
+}
+
+int drift_contract_dev(drift_ctx *ctx, const drift_policy *p, const drift_contraction *op,
+                       const double *d_a, const double *d_b, double *d_c, uint64_t *d_rng_state,
+                       void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || !op) return fail(DRIFT_EINVAL, "null argument");
+    rc = check_contraction(*op);
+    if (rc) return fail(rc, "bad contraction");
+    if (op->batch * op->rows * op->cols == 0) return DRIFT_OK;
+    if (!d_c || (op->depth > 0 && (!d_a || !d_b))) return fail(DRIFT_EINVAL, "null buffer");
+    if (stochastic_acc(p) && !d_rng_state)
+        return fail(DRIFT_EINVAL, "stochastic accumulation needs d_rng_state");
+    ContractDesc d{*op, d_a, d_b, d_c, nullptr};
+    rc = launch_contract(ctx->ws, p, d, d_rng_state, pick(ctx, stream));
+    return rc ? fail(rc, "contraction launch") : DRIFT_OK;
 }
 
 int drift_radix_hist_dev(drift_ctx *ctx, const double *d_got, const double *d_exact, int64_t n,

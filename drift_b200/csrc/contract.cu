@@ -1,0 +1,522 @@
+// contract.cu — batched, ragged and causal contractions, and every
+// contraction with a stochastically rounded accumulator.
+//
+// Output (t, i, o) of a contraction is Dot.dot over the window k in
+// [lo(i), lo(i) + n(i)) of A[t, i, k] * B[t, o, k], the term at k = lo(i)
+// first (Dot.dot's index 0). The windows are AttnPass's
+// (java/src/main/java/io/drift/train/AttnPass.java): the whole depth for the
+// score and dProb matmuls (:245-255, :373-381), the prefix [0, i] for the
+// context and dq matmuls (:283-288, :412-417), the suffix [i, depth) for dv
+// and dk (:382-388, :419-424). Causal contractions write 0.0 for o > i
+// without a dot, as those loops do. The result is dot * alpha (the score
+// scale, :248) when alpha is not 1, plus bias[o] for a linear, added into C
+// for an accumulating dInput (:478-484).
+//
+// One output per thread, operands through the read-only cache with any
+// strides: the attention shapes are small and ragged, and every order needs
+// its own per-row tree.
+//
+// Stochastic accumulation. Dot.round with STOCHASTIC (Dot.java:171-175)
+// draws from the Rng the caller shares across dots, in the order the dots run
+// ((t, i, o) loops) and, inside a dot, in its evaluation order, and only when
+// the sum is not exactly representable. So dot j starts drawing at D_j = the
+// draws of dots 0..j-1, which the earlier dots' data decide. The engine finds
+// the D_j by a fixed point: it predicts every dot's count, scans the
+// predictions into offsets, computes all dots in parallel from those offsets
+// (splitmix64 is counter-based, so any draw is available directly), and
+// records each dot's true count. If the scan of the true counts gives back
+// the offsets that were used, every dot started at the right draw (by
+// induction from D_0 = 0) and the result is the sequential one. Otherwise the
+// new offsets are used and the pass repeats. The first prediction — one draw
+// per rounding the order performs — is exact unless some sum is exactly
+// representable, so one pass usually settles it. After a bounded number of
+// passes the dots are walked in order by one thread, which is correct for any
+// data. Nothing spins: each pass is a separate launch and the host reads a
+// flag between them.
+#include <algorithm>
+
+#include "codec.cuh"
+#include "internal.h"
+
+namespace drift {
+
+struct ContractArgs {
+    int64_t batch, rows, cols, depth;
+    const double *A;
+    int64_t a_batch, a_row, a_k;
+    const double *B;
+    int64_t b_batch, b_col, b_k;
+    double *C;
+    int64_t c_batch, c_row, c_col;
+    const double *bias;
+    double alpha;
+    int window, causal, accumulate, order;
+    int64_t acc_block;
+    const uint64_t *state;   // Rng state before the first draw (stochastic only)
+    const int64_t *offsets;  // first draw index of each dot, (t, i, o) order
+    uint32_t *counts;        // draws each dot made
+};
+
+__device__ __forceinline__ void window_of(const ContractArgs &g, int64_t i, int64_t &lo,
+                                          int64_t &n) {
+    if (g.window == DRIFT_WINDOW_PREFIX) {
+        lo = 0;
+        n = i + 1;
+    } else if (g.window == DRIFT_WINDOW_SUFFIX) {
+        lo = i;
+        n = g.depth - i;
+    } else {
+        lo = 0;
+        n = g.depth;
+    }
+}
+
+// Dot.round(x, acc, STOCHASTIC, rng) (Dot.java:141-182), drawing the
+// (idx + cnt)-th number of the stream only when the fraction is non-zero.
+template <int ACC>
+__device__ __forceinline__ double sr_round(double x, uint64_t state, uint64_t idx, uint32_t &cnt) {
+    using F = AccFmt<ACC>;
+    if (x == 0.0 || isnan(x)) return x;
+    const double ax = fabs(x);
+    if (isinf(ax)) return copysign(F::max(), x);
+    int e = java_get_exponent(ax);
+    if (e < F::min_exp) e = F::min_exp;
+    const int q = e - F::mant;
+    const double scaled = __dmul_rn(ax, pow2(-q));  // exact
+    const double fl = floor(scaled);
+    const double frac = __dsub_rn(scaled, fl);
+    double m = fl;
+    if (frac != 0.0) {
+        const uint64_t u = draw_u53(state, idx + cnt);
+        cnt++;
+        if (__dmul_rn((double)u, 0x1p-53) < frac) m = fl + 1.0;
+    }
+    double r = __dmul_rn(m, pow2(q));
+    if (r > F::max()) r = F::max();
+    return copysign(r, x);
+}
+
+// The accumulator's rounding after each add (Dot.java:43-63): identity for
+// FP64, (float) for FP32, Dot.round for FP16/BF16.
+template <int ACC, int RM> struct ExactRounder {
+    __device__ double operator()(double t) { return AccRound<ACC, RM>::exact(t); }
+};
+
+template <int ACC> struct SrRounder {
+    uint64_t state, idx;
+    uint32_t cnt;
+    __device__ double operator()(double t) { return sr_round<ACC>(t, state, idx, cnt); }
+};
+
+// Dot.dot (Dot.java:26-121) over n terms a[k*a_k] * b[k*b_k], any order.
+template <int ACC, class R>
+__device__ double dot_any(const ContractArgs &g, const double *a, const double *b, int64_t n,
+                          R &rnd) {
+    auto term = [&](int64_t k) { return __dmul_rn(__ldg(a + k * g.a_k), __ldg(b + k * g.b_k)); };
+    auto fwd = [&](int64_t from, int64_t count) {  // Dot.forward (:37-68)
+        double s = 0.0;
+        for (int64_t k = from; k < from + count; k++) s = rnd(__dadd_rn(s, term(k)));
+        return s;
+    };
+    if (g.order == DRIFT_SEQUENTIAL) return fwd(0, n);
+    if (g.order == DRIFT_REVERSED) {  // Dot.backward (:70-84)
+        double s = 0.0;
+        for (int64_t k = n - 1; k >= 0; k--) s = rnd(__dadd_rn(s, term(k)));
+        return s;
+    }
+    if (g.order == DRIFT_BLOCKED) {  // Dot.blocked (:104-121)
+        double total = 0.0;
+        for (int64_t start = 0; start < n; start += g.acc_block) {
+            const double partial = fwd(start, min(g.acc_block, n - start));
+            total = ACC == DRIFT_ACC_FP64 ? __dadd_rn(total, partial)
+                                          : (double)__double2float_rn(__dadd_rn(total, partial));
+        }
+        return total;
+    }
+    // Dot.pairwise (:86-102): halves of count >>> 1, leaves of at most 8,
+    // left subtree, right subtree, then the combine. An explicit stack of
+    // pending nodes (count < 0 marks a combine) and of finished values; for
+    // n < 2^31 the tree is at most 28 splits deep.
+    if (n <= 8) return fwd(0, n);
+    int64_t todo_off[60], todo_cnt[60];
+    double vals[32];
+    int tp = 1, vp = 0;
+    todo_off[0] = 0;
+    todo_cnt[0] = n;
+    while (tp > 0) {
+        tp--;
+        const int64_t off = todo_off[tp], cnt = todo_cnt[tp];
+        if (cnt < 0) {
+            vp--;
+            vals[vp - 1] = rnd(__dadd_rn(vals[vp - 1], vals[vp]));
+        } else if (cnt <= 8) {
+            vals[vp++] = fwd(off, cnt);
+        } else {
+            const int64_t half = cnt >> 1;
+            todo_cnt[tp++] = -1;
+            todo_off[tp] = off + half;
+            todo_cnt[tp++] = cnt - half;
+            todo_off[tp] = off;
+            todo_cnt[tp++] = half;
+        }
+    }
+    return vals[0];
+}
+
+// Leaves of Dot.pairwise's tree over n terms. Node sizes on one level differ
+// by at most one, so two (size, count) slots carry a level.
+__device__ __forceinline__ int64_t pairwise_leaves(int64_t n) {
+    int64_t s0 = n, c0 = 1, c1 = 0, leaves = 0;  // sizes s0 and s0 + 1
+    while (c0 + c1 > 0) {
+        int64_t t0 = 0, t1 = 0;
+        const int64_t ns0 = s0 >> 1;  // children of s0: ns0 and s0 - ns0
+        auto add = [&](int64_t size, int64_t count) {
+            if (count == 0) return;
+            if (size == ns0) t0 += count;
+            else t1 += count;  // size == ns0 + 1
+        };
+        int64_t sz[2] = {s0, s0 + 1}, ct[2] = {c0, c1};
+        for (int j = 0; j < 2; j++) {
+            if (ct[j] == 0) continue;
+            if (sz[j] <= 8) {
+                leaves += ct[j];
+            } else {
+                add(sz[j] >> 1, ct[j]);
+                add(sz[j] - (sz[j] >> 1), ct[j]);
+            }
+        }
+        s0 = ns0;
+        c0 = t0;
+        c1 = t1;
+    }
+    return leaves;
+}
+
+// Draws a dot of n terms makes when every sum is inexact: one per rounding.
+__device__ __forceinline__ int64_t predicted_draws(int order, int64_t n) {
+    if (n <= 0) return 0;
+    return order == DRIFT_PAIRWISE ? n + pairwise_leaves(n) - 1 : n;
+}
+
+__device__ __forceinline__ void store(const ContractArgs &g, double *c, int64_t o, double v) {
+    if (g.alpha != 1.0) v = __dmul_rn(v, g.alpha);
+    if (g.bias) v = __dadd_rn(v, g.bias[o]);
+    if (g.accumulate) v = __dadd_rn(*c, v);
+    *c = v;
+}
+
+template <int ACC, int RM>
+__global__ void __launch_bounds__(128) contract_kernel(const ContractArgs g) {
+    const int64_t total = g.batch * g.rows * g.cols;
+    for (int64_t out = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; out < total;
+         out += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = out % g.cols, ti = out / g.cols;
+        const int64_t i = ti % g.rows, t = ti / g.rows;
+        double *c = g.C + t * g.c_batch + i * g.c_row + o * g.c_col;
+        if (g.causal && o > i) {
+            *c = 0.0;
+            continue;
+        }
+        int64_t lo, n;
+        window_of(g, i, lo, n);
+        ExactRounder<ACC, RM> rnd;
+        const double v = dot_any<ACC>(g, g.A + t * g.a_batch + i * g.a_row + lo * g.a_k,
+                                      g.B + t * g.b_batch + o * g.b_col + lo * g.b_k, n, rnd);
+        store(g, c, o, v);
+    }
+}
+
+// The value of output `out` before it meets C (dot * alpha + bias), drawing
+// from index idx on; 0.0 and no draws for a masked causal output.
+template <int ACC>
+__device__ __forceinline__ double sr_output(const ContractArgs &g, int64_t out, uint64_t idx,
+                                            uint32_t &cnt) {
+    const int64_t o = out % g.cols, i = (out / g.cols) % g.rows, t = out / g.cols / g.rows;
+    cnt = 0;
+    if (g.causal && o > i) return 0.0;
+    int64_t lo, n;
+    window_of(g, i, lo, n);
+    SrRounder<ACC> rnd{*g.state, idx, 0};
+    double v = dot_any<ACC>(g, g.A + t * g.a_batch + i * g.a_row + lo * g.a_k,
+                            g.B + t * g.b_batch + o * g.b_col + lo * g.b_k, n, rnd);
+    cnt = rnd.cnt;
+    if (g.alpha != 1.0) v = __dmul_rn(v, g.alpha);
+    if (g.bias) v = __dadd_rn(v, g.bias[o]);
+    return v;
+}
+
+// One speculative pass: every dot from its offset into the scratch values,
+// its true count recorded. C is written once, after the offsets settle.
+template <int ACC>
+__global__ void __launch_bounds__(128) contract_sr_kernel(const ContractArgs g, double *vals) {
+    const int64_t total = g.batch * g.rows * g.cols;
+    for (int64_t out = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; out < total;
+         out += (int64_t)gridDim.x * blockDim.x) {
+        uint32_t cnt;
+        vals[out] = sr_output<ACC>(g, out, (uint64_t)g.offsets[out], cnt);
+        g.counts[out] = cnt;
+    }
+}
+
+// The dots in order, one thread: the fallback that is correct for any data.
+template <int ACC>
+__global__ void contract_sr_serial_kernel(const ContractArgs g, double *vals,
+                                          uint64_t *total_draws) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    uint64_t idx = 0;
+    const int64_t total = g.batch * g.rows * g.cols;
+    for (int64_t out = 0; out < total; out++) {
+        uint32_t cnt;
+        vals[out] = sr_output<ACC>(g, out, idx, cnt);
+        idx += cnt;
+    }
+    *total_draws = idx;
+}
+
+// C from the settled values: 0.0 where the causal mask hides the output,
+// else the value, added into C for an accumulating contraction.
+__global__ void contract_apply_kernel(const ContractArgs g, const double *vals) {
+    const int64_t total = g.batch * g.rows * g.cols;
+    for (int64_t out = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; out < total;
+         out += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = out % g.cols, i = (out / g.cols) % g.rows, t = out / g.cols / g.rows;
+        double *c = g.C + t * g.c_batch + i * g.c_row + o * g.c_col;
+        if (g.causal && o > i) *c = 0.0;
+        else *c = g.accumulate ? __dadd_rn(*c, vals[out]) : vals[out];
+    }
+}
+
+// ------------------------------------------------------------------ offsets
+
+constexpr int kScanThreads = 1024;
+
+// Per-block sums of n uint32 counts (block b covers [b*chunk, (b+1)*chunk)).
+__global__ void __launch_bounds__(kScanThreads) block_sums_kernel(const uint32_t *counts, int64_t n,
+                                                                  int64_t chunk, uint64_t *sums) {
+    __shared__ uint64_t s_part[kScanThreads / 32];
+    const int64_t lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
+    uint64_t acc = 0;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) acc += counts[i];
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint64_t t = 0;
+        for (int w = 0; w < kScanThreads / 32; w++) t += s_part[w];
+        sums[blockIdx.x] = t;
+    }
+}
+
+// Exclusive scan of the block sums in place (one thread; a few thousand
+// values at most); also writes the grand total to sums[nb].
+__global__ void scan_sums_kernel(uint64_t *sums, int64_t nb) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    uint64_t run = 0;
+    for (int64_t b = 0; b < nb; b++) {
+        const uint64_t v = sums[b];
+        sums[b] = run;
+        run += v;
+    }
+    sums[nb] = run;
+}
+
+// offsets[i] = exclusive prefix of counts, block by block; raises *mismatch
+// if it differs from the offsets already there (the ones the pass used).
+__global__ void __launch_bounds__(kScanThreads) apply_offsets_kernel(const uint32_t *counts,
+                                                                     int64_t n, int64_t chunk,
+                                                                     const uint64_t *sums,
+                                                                     int64_t *offsets,
+                                                                     int *mismatch) {
+    __shared__ uint64_t s_warp[kScanThreads / 32];
+    __shared__ uint64_t s_carry;
+    const int64_t lo = blockIdx.x * chunk, hi = min(n, lo + chunk);
+    if (threadIdx.x == 0) s_carry = sums[blockIdx.x];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    bool differ = false;
+    for (int64_t base = lo; base < hi; base += blockDim.x) {
+        const int64_t i = base + threadIdx.x;
+        const uint64_t v = i < hi ? counts[i] : 0;
+        uint64_t incl = v;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (lane == 31) s_warp[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            const uint64_t w = s_warp[lane];
+            uint64_t wi = w;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t t = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += t;
+            }
+            s_warp[lane] = wi - w;
+        }
+        __syncthreads();
+        const uint64_t carry = s_carry;
+        if (i < hi) {
+            const int64_t off = (int64_t)(carry + s_warp[warp] + incl - v);
+            if (offsets[i] != off) differ = true;
+            offsets[i] = off;
+        }
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) s_carry = carry + s_warp[warp] + incl;
+        __syncthreads();
+    }
+    if (differ) atomicOr(mismatch, 1);
+}
+
+// The first prediction of every dot's draw count.
+__global__ void predict_counts_kernel(const ContractArgs g, uint32_t *counts) {
+    const int64_t total = g.batch * g.rows * g.cols;
+    for (int64_t out = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; out < total;
+         out += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = out % g.cols, i = (out / g.cols) % g.rows;
+        int64_t lo, n;
+        window_of(g, i, lo, n);
+        counts[out] = (g.causal && o > i) ? 0u : (uint32_t)predicted_draws(g.order, n);
+    }
+}
+
+__global__ void advance_state_kernel(uint64_t *state, const uint64_t *total) {
+    *state += *total * kGolden;
+}
+
+// ------------------------------------------------------------------ launcher
+
+constexpr int kMaxSrPasses = 8;
+
+static unsigned grid_of(int64_t total) {
+    const int64_t blocks = (total + 127) / 128;
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>(blocks, 148 * 64));
+}
+
+static ContractArgs args_of(const drift_policy *p, const ContractDesc &d) {
+    ContractArgs g{};
+    g.batch = d.op.batch;
+    g.rows = d.op.rows;
+    g.cols = d.op.cols;
+    g.depth = d.op.depth;
+    g.A = d.a + d.op.a_off;
+    g.a_batch = d.op.a_batch;
+    g.a_row = d.op.a_row;
+    g.a_k = d.op.a_k;
+    g.B = d.b + d.op.b_off;
+    g.b_batch = d.op.b_batch;
+    g.b_col = d.op.b_col;
+    g.b_k = d.op.b_k;
+    g.C = d.c + d.op.c_off;
+    g.c_batch = d.op.c_batch;
+    g.c_row = d.op.c_row;
+    g.c_col = d.op.c_col;
+    g.bias = d.bias;
+    g.alpha = d.op.alpha;
+    g.window = d.op.window;
+    g.causal = d.op.causal;
+    g.accumulate = d.op.accumulate;
+    g.order = p->order;
+    g.acc_block = std::max<int64_t>(1, p->acc_block);
+    return g;
+}
+
+int check_contraction(const drift_contraction &op) {
+    if (op.batch < 0 || op.rows < 0 || op.cols < 0 || op.depth < 0) return DRIFT_EINVAL;
+    if (op.depth > 0x7fffffffLL) return DRIFT_EUNSUPPORTED;
+    if (op.window != DRIFT_WINDOW_FULL && op.window != DRIFT_WINDOW_PREFIX &&
+        op.window != DRIFT_WINDOW_SUFFIX)
+        return DRIFT_EINVAL;
+    if (op.window != DRIFT_WINDOW_FULL && op.rows > op.depth) return DRIFT_EINVAL;
+    if ((op.causal | op.accumulate) & ~1 || op.reserved != 0) return DRIFT_EINVAL;
+    if (op.a_off < 0 || op.b_off < 0 || op.c_off < 0) return DRIFT_EINVAL;
+    return DRIFT_OK;
+}
+
+static bool stochastic(const drift_policy *p) {
+    return p->acc_rounding == DRIFT_STOCHASTIC &&
+           (p->acc == DRIFT_ACC_FP16 || p->acc == DRIFT_ACC_BF16);
+}
+
+int launch_contract(Workspace &ws, const drift_policy *p, const ContractDesc &d, uint64_t *d_state,
+                    cudaStream_t st) {
+    int rc = check_contraction(d.op);
+    if (rc) return rc;
+    const int64_t total = d.op.batch * d.op.rows * d.op.cols;
+    if (total == 0) return DRIFT_OK;
+    if (p->acc < DRIFT_ACC_FP64 || p->acc > DRIFT_ACC_BF16 || p->order < DRIFT_SEQUENTIAL ||
+        p->order > DRIFT_BLOCKED)
+        return DRIFT_EINVAL;
+    ContractArgs g = args_of(p, d);
+    const unsigned grid = grid_of(total);
+
+    if (!stochastic(p)) {
+        const bool tr = p->acc_rounding == DRIFT_TRUNCATE;
+        switch (p->acc) {
+            case DRIFT_ACC_FP64:
+                contract_kernel<DRIFT_ACC_FP64, DRIFT_NEAREST_EVEN><<<grid, 128, 0, st>>>(g);
+                break;
+            case DRIFT_ACC_FP32:
+                contract_kernel<DRIFT_ACC_FP32, DRIFT_NEAREST_EVEN><<<grid, 128, 0, st>>>(g);
+                break;
+            case DRIFT_ACC_FP16:
+                if (tr) contract_kernel<DRIFT_ACC_FP16, DRIFT_TRUNCATE><<<grid, 128, 0, st>>>(g);
+                else contract_kernel<DRIFT_ACC_FP16, DRIFT_NEAREST_EVEN><<<grid, 128, 0, st>>>(g);
+                break;
+            default:
+                if (tr) contract_kernel<DRIFT_ACC_BF16, DRIFT_TRUNCATE><<<grid, 128, 0, st>>>(g);
+                else contract_kernel<DRIFT_ACC_BF16, DRIFT_NEAREST_EVEN><<<grid, 128, 0, st>>>(g);
+        }
+        return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+    }
+
+    if (!d_state) return DRIFT_EINVAL;  // Java: NullPointerException on the first draw
+    const int64_t chunk = 64 * kScanThreads;
+    const int64_t nb = (total + chunk - 1) / chunk;
+    const size_t count_bytes = (total * sizeof(uint32_t) + 7) & ~7ULL;
+    const size_t bytes = total * sizeof(int64_t) + total * sizeof(double) + count_bytes +
+                         (nb + 2) * sizeof(uint64_t) + 64;
+    char *w = (char *)ws.get(bytes, st);
+    if (!w) return DRIFT_ENOMEM;
+    int64_t *offsets = (int64_t *)w;
+    double *vals = (double *)(w + total * sizeof(int64_t));
+    uint32_t *counts = (uint32_t *)(w + total * (sizeof(int64_t) + sizeof(double)));
+    uint64_t *sums = (uint64_t *)((char *)counts + count_bytes);
+    int *mismatch = (int *)(sums + nb + 2);
+    uint64_t *total_draws = sums + nb;
+    g.state = d_state;
+    g.offsets = offsets;
+    g.counts = counts;
+    const bool fp16 = p->acc == DRIFT_ACC_FP16;
+
+    auto scan = [&]() {
+        cudaMemsetAsync(mismatch, 0, sizeof(int), st);
+        block_sums_kernel<<<(unsigned)nb, kScanThreads, 0, st>>>(counts, total, chunk, sums);
+        scan_sums_kernel<<<1, 32, 0, st>>>(sums, nb);
+        apply_offsets_kernel<<<(unsigned)nb, kScanThreads, 0, st>>>(counts, total, chunk, sums,
+                                                                    offsets, mismatch);
+    };
+    predict_counts_kernel<<<grid, 128, 0, st>>>(g, counts);
+    cudaMemsetAsync(offsets, 0xff, total * sizeof(int64_t), st);  // differs from any offset
+    scan();
+    bool settled = false;
+    for (int pass = 0; pass < kMaxSrPasses && !settled; pass++) {
+        if (fp16) contract_sr_kernel<DRIFT_ACC_FP16><<<grid, 128, 0, st>>>(g, vals);
+        else contract_sr_kernel<DRIFT_ACC_BF16><<<grid, 128, 0, st>>>(g, vals);
+        scan();
+        int flag = 1;
+        if (cudaMemcpyAsync(&flag, mismatch, sizeof(int), cudaMemcpyDeviceToHost, st) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
+            return DRIFT_ECUDA;
+        settled = flag == 0;
+    }
+    if (!settled) {
+        if (fp16) contract_sr_serial_kernel<DRIFT_ACC_FP16><<<1, 1, 0, st>>>(g, vals, total_draws);
+        else contract_sr_serial_kernel<DRIFT_ACC_BF16><<<1, 1, 0, st>>>(g, vals, total_draws);
+    }
+    contract_apply_kernel<<<grid, 128, 0, st>>>(g, vals);
+    advance_state_kernel<<<1, 1, 0, st>>>(d_state, total_draws);
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+}
+
+}  // namespace drift

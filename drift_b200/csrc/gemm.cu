@@ -556,7 +556,7 @@ int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int6
     if (p->acc < 0 || p->acc > 3 || p->order < 0 || p->order > 3) return DRIFT_EINVAL;
     const bool narrow = p->acc == DRIFT_ACC_FP16 || p->acc == DRIFT_ACC_BF16;
     if (narrow && (p->acc_rounding < 0 || p->acc_rounding > 2)) return DRIFT_EINVAL;
-    if (narrow && p->acc_rounding == DRIFT_STOCHASTIC) return DRIFT_EINVAL;  // gemm_sr.cu
+    if (narrow && p->acc_rounding == DRIFT_STOCHASTIC) return DRIFT_EINVAL;  // contract.cu
     if (M == 0 || N == 0) return DRIFT_OK;
     const int64_t gx = (N + BN - 1) / BN, gy = (M + BM - 1) / BM;
     if (gx > 0x7fffffffLL || gy > 65535) return DRIFT_EINVAL;

@@ -65,10 +65,18 @@ int launch_radix_pass(const double *got, const double *exact, int64_t n, int pas
                       unsigned long long *state, unsigned long long *hist, cudaStream_t st);
 int launch_radix_select(int pass, const unsigned long long *hist, unsigned long long *state,
                         cudaStream_t st);
-int launch_gemm_sr(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M,
-                   int64_t N, int64_t K, const double *A, int64_t a_rs, int64_t a_ks,
-                   const double *B, int64_t b_rs, int64_t b_ks, const double *bias, double *C,
-                   int64_t c_rs, uint64_t *d_state, cudaStream_t st);
+// contract.cu: a contraction with its buffers (a, b, c before the op's
+// offsets) and an optional bias of `cols` values (drift_gemm's linears).
+struct ContractDesc {
+    drift_contraction op;
+    const double *a;
+    const double *b;
+    double *c;
+    const double *bias;
+};
+int check_contraction(const drift_contraction &op);
+int launch_contract(Workspace &ws, const drift_policy *p, const ContractDesc &d, uint64_t *d_state,
+                    cudaStream_t st);
 int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,

@@ -262,6 +262,46 @@ def gemm(p: NumericPolicy, M: int, N: int, K: int, A, a_off: int, a_rs: int, a_k
     return out
 
 
+class Window(IntEnum):
+    """The k window of row i of a contraction (include/drift_b200.h)."""
+
+    FULL = 0     # [0, depth): score and dProb matmuls (AttnPass.java:245-255, :373-381)
+    PREFIX = 1   # [0, i]: context and dq matmuls (:283-288, :412-417)
+    SUFFIX = 2   # [i, depth): dv and dk matmuls (:382-388, :419-424)
+
+
+def contraction(*, rows: int, cols: int, depth: int, a_row: int, a_k: int, b_col: int, b_k: int,
+                c_row: int, batch: int = 1, a_off: int = 0, a_batch: int = 0, b_off: int = 0,
+                b_batch: int = 0, c_off: int = 0, c_batch: int = 0, c_col: int = 1,
+                alpha: float = 1.0, window: Window = Window.FULL, causal: bool = False,
+                accumulate: bool = False) -> "_lib.DriftContraction":
+    """A drift_contraction: output (t, i, o) at C[c_off + t*c_batch + i*c_row +
+    o*c_col] is Dot.dot(A, a_off + t*a_batch + i*a_row + lo*a_k, a_k,
+    B, b_off + t*b_batch + o*b_col + lo*b_k, b_k, n) * alpha (added into C when
+    accumulating) over row i's window (lo, n); 0.0 for o > i when causal."""
+    return _lib.DriftContraction(batch, rows, cols, depth, a_off, a_batch, a_row, a_k, b_off,
+                                 b_batch, b_col, b_k, c_off, c_batch, c_row, c_col, float(alpha),
+                                 int(window), int(bool(causal)), int(bool(accumulate)), 0)
+
+
+def contract(p: NumericPolicy, op, A: np.ndarray, B: np.ndarray, C: np.ndarray,
+             rng: Optional[Rng] = None) -> np.ndarray:
+    """One contraction over host arrays (flat float64), C updated in place
+    and returned: the Dot.dot loops of AttnPass.java:245-427 in one call."""
+    A = np.ascontiguousarray(np.asarray(A, dtype=np.float64)).reshape(-1)
+    B = np.ascontiguousarray(np.asarray(B, dtype=np.float64)).reshape(-1)
+    if C.dtype != np.float64 or not C.flags.c_contiguous:
+        raise TypeError("C must be a contiguous float64 array")
+    st = _state_in(rng)
+    pc = p.to_c()
+    _lib.check(_lib.load().drift_contract(
+        _lib.Context.current().handle, ctypes.byref(pc), ctypes.byref(op), A.ctypes.data, A.size,
+        B.ctypes.data, B.size, C.ctypes.data, C.size,
+        ctypes.byref(st) if st is not None else None))
+    _state_out(rng, st)
+    return C
+
+
 # ----------------------------------------------------------- device-resident calls
 # These take torch CUDA tensors (float64) and run on torch's current stream.
 
@@ -298,6 +338,17 @@ def gemm_dev(p: NumericPolicy, A, B, C, *, M=None, N=None, K=None, a_rs=None, a_
     _lib.check(_lib.load().drift_gemm_dev(ctx.handle, ctypes.byref(pc), M, N, K, _tptr(A), a_rs,
                                           a_ks, _tptr(B), b_rs, b_ks, _tptr(bias), _tptr(C), c_rs,
                                           _tptr(d_rng_state), _stream_ptr(stream)))
+
+
+def contract_dev(p: NumericPolicy, op, A, B, C, *, d_rng_state=None, stream=None,
+                 ctx=None) -> None:
+    """One contraction on device tensors (float64, addressed through `op`'s
+    offsets and strides); a stochastic accumulator needs d_rng_state."""
+    ctx = ctx or _lib.Context.current()
+    pc = p.to_c()
+    _lib.check(_lib.load().drift_contract_dev(ctx.handle, ctypes.byref(pc), ctypes.byref(op),
+                                              _tptr(A), _tptr(B), _tptr(C), _tptr(d_rng_state),
+                                              _stream_ptr(stream)))
 
 
 def quantize_dev(p: NumericPolicy, f: Optional[MiniFloat], rm: Rounding, src, dst, *,

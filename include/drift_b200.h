@@ -314,6 +314,51 @@ DRIFT_API int drift_radix_select_dev(drift_ctx *ctx, int pass,
                                      void *stream);
 
 /* ----------------------------------------------------------- diagnostics */
+/*
+ * A batched contraction with per-row windows: the attention matmuls of
+ * AttnPass (java/.../train/AttnPass.java:245-290, :373-427), and a batched
+ * drift_gemm. For t < batch, i < rows, o < cols the output
+ *   C[c_off + t*c_batch + i*c_row + o*c_col]
+ * is Dot.dot(A, a_off + t*a_batch + i*a_row + lo*a_k, a_k,
+ *            B, b_off + t*b_batch + o*b_col + lo*b_k, b_k, n, p, rng)
+ * times alpha (when alpha != 1: the score scale, :248), added into C when
+ * `accumulate` is set (dInput into dx, :478-484). The window (lo, n) of row i:
+ *   DRIFT_WINDOW_FULL    lo = 0, n = depth (scores, dProb: :245-255, :373-381)
+ *   DRIFT_WINDOW_PREFIX  lo = 0, n = i + 1 (context, dq: :283-288, :412-417)
+ *   DRIFT_WINDOW_SUFFIX  lo = i, n = depth - i (dv, dk: :382-388, :419-424)
+ * PREFIX and SUFFIX need rows <= depth. With `causal` set, outputs with
+ * o > i are written 0.0 and take no dot (and no draws). Dots run, and a
+ * stochastic accumulator draws, in (t, i, o) order. C must not overlap A or B.
+ */
+#define DRIFT_WINDOW_FULL   0
+#define DRIFT_WINDOW_PREFIX 1
+#define DRIFT_WINDOW_SUFFIX 2
+typedef struct drift_contraction {
+    int64_t batch, rows, cols, depth;
+    int64_t a_off, a_batch, a_row, a_k;
+    int64_t b_off, b_batch, b_col, b_k;
+    int64_t c_off, c_batch, c_row, c_col;
+    double alpha;
+    int32_t window;
+    int32_t causal;
+    int32_t accumulate;
+    int32_t reserved;    /* must be 0 */
+} drift_contraction;
+
+/* Host buffers a[a_len], b[b_len], c[c_len] (Java arrays): every element the
+ * contraction reaches must lie inside them, or DRIFT_EINVAL. c is read
+ * (accumulate) and written in place. The Rng state travels as with
+ * drift_gemm. */
+DRIFT_API int drift_contract(drift_ctx *ctx, const drift_policy *p, const drift_contraction *op,
+                   const double *a, int64_t a_len, const double *b, int64_t b_len,
+                   double *c, int64_t c_len, uint64_t *rng_state);
+/* Device buffers on `stream`; the Rng state is the device uint64
+ * *d_rng_state, needed only by a stochastic accumulator. */
+DRIFT_API int drift_contract_dev(drift_ctx *ctx, const drift_policy *p,
+                       const drift_contraction *op, const double *d_a,
+                       const double *d_b, double *d_c, uint64_t *d_rng_state,
+                       void *stream);
+
 /* No counterpart in the reference: measures the FP64 pipe's DMUL+DADD issue
  * rate on the context's device (operations per second), the denominator of
  * the contraction's roofline. Takes a few milliseconds. */

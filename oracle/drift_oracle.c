@@ -561,6 +561,43 @@ int o_gemm(const drift_policy *p, int64_t M, int64_t N, int64_t K,
     return err;
 }
 
+/* ------------------------------------------------------------ attention loops */
+
+/* AttnPass's score loop (../train/AttnPass.java:245-255): dot over the whole
+ * depth for s <= i, times scoreScale, 0.0 for s > i; dProb (:373-381) the
+ * same without the scale. Context and dq (:283-288, :412-417): n = i + 1
+ * from k = 0. dv and dk (:382-388, :419-424): n = t - s from k = s. The
+ * dInput accumulation (:478-484): dx += dot. */
+int o_contract(const drift_policy *p, const drift_contraction *op, const double *A,
+               const double *B, double *C, uint64_t *rng_state) {
+    for (int64_t t = 0; t < op->batch; t++) {
+        for (int64_t i = 0; i < op->rows; i++) {
+            for (int64_t o = 0; o < op->cols; o++) {
+                double *c = C + op->c_off + t * op->c_batch + i * op->c_row + o * op->c_col;
+                if (op->causal && o > i) {
+                    *c = 0.0;
+                    continue;
+                }
+                int64_t lo = 0, n = op->depth;
+                if (op->window == DRIFT_WINDOW_PREFIX) n = i + 1;
+                if (op->window == DRIFT_WINDOW_SUFFIX) {
+                    lo = i;
+                    n = op->depth - i;
+                }
+                int err = 0;
+                double v = o_dot(A, op->a_off + t * op->a_batch + i * op->a_row + lo * op->a_k,
+                                 op->a_k, B,
+                                 op->b_off + t * op->b_batch + o * op->b_col + lo * op->b_k,
+                                 op->b_k, n, p, rng_state, &err);
+                if (err) return err;
+                if (op->alpha != 1.0) v = v * op->alpha;
+                *c = op->accumulate ? *c + v : v;
+            }
+        }
+    }
+    return DRIFT_OK;
+}
+
 /* ------------------------------------------------------------ java.util.Random */
 
 #define JR_MULT 0x5DEECE66DULL

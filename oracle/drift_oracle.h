@@ -58,6 +58,13 @@ int o_gemm(const drift_policy *p, int64_t M, int64_t N, int64_t K,
            const double *bias, double *C, int64_t c_rs, uint64_t *rng_state,
            int threads);
 
+/* The (t, i, o) loops of AttnPass over Dot.dot
+ * (java/.../train/AttnPass.java:245-290, :373-427) for one drift_contraction:
+ * row i's window, 0.0 for causal o > i, the score scale, the accumulating
+ * add of dInput (:478-484). */
+int o_contract(const drift_policy *p, const drift_contraction *op, const double *A,
+               const double *B, double *C, uint64_t *rng_state);
+
 /* java.util.Random as specified by its Javadoc (LCG 0x5DEECE66D, polar
  * nextGaussian with StrictMath.sqrt/log), used to regenerate the reference's
  * DotSweep inputs (java/.../tools/DotSweep.java:124-130). log and exp come

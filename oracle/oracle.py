@@ -83,6 +83,7 @@ def lib() -> ctypes.CDLL:
         L.o_dot.restype = d
         L.o_gemm.argtypes = [P(OraclePolicy), i64, i64, i64, vp, i64, i64, i64, vp, i64, i64,
                              i64, vp, vp, i64, P(u64), ctypes.c_int]
+        L.o_contract.argtypes = [P(OraclePolicy), vp, vp, vp, vp, P(u64)]
         L.o_dotsweep_fill.argtypes = [vp, vp, i64, i64]
         _LIB = L
     return _LIB
@@ -188,6 +189,29 @@ def gemm(p: OraclePolicy, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks, b
                         b_rs, b_ks, bptr, C.ctypes.data, c_rs,
                         None if r is None else ctypes.byref(r), threads))
     return C, (None if r is None else r.value)
+
+
+class OracleContraction(ctypes.Structure):
+    """Byte layout of drift_contraction (include/drift_b200.h)."""
+
+    _fields_ = [(n, ctypes.c_int64) for n in (
+        "batch", "rows", "cols", "depth", "a_off", "a_batch", "a_row", "a_k", "b_off", "b_batch",
+        "b_col", "b_k", "c_off", "c_batch", "c_row", "c_col")] + [
+        ("alpha", ctypes.c_double), ("window", ctypes.c_int32), ("causal", ctypes.c_int32),
+        ("accumulate", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+def contract(p: OraclePolicy, op, A, B, C, rng_state=None):
+    """AttnPass's loops for one contraction (op: any ctypes structure with
+    drift_contraction's layout). C (flat float64) is updated in place.
+    Returns the new rng state."""
+    A = np.ascontiguousarray(A, dtype=np.float64)
+    B = np.ascontiguousarray(B, dtype=np.float64)
+    assert C.dtype == np.float64 and C.flags.c_contiguous
+    r = _rng(rng_state)
+    _check(lib().o_contract(ctypes.byref(p), ctypes.addressof(op), _dptr(A), _dptr(B), C.ctypes.data,
+                            None if r is None else ctypes.byref(r)))
+    return None if r is None else r.value
 
 
 def dotsweep_fill(n: int, seed: int):

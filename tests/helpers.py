@@ -43,3 +43,51 @@ def with_edges(x: np.ndarray, rs: np.random.Generator, nan: bool = True) -> np.n
     for k, p in enumerate(pos):
         x[p] = specials[k % len(specials)]
     return x
+
+
+def opolicy(p):
+    """The oracle's copy of a drift_b200 NumericPolicy."""
+    from oracle import oracle as O
+
+    c = p.to_c()
+    return O.OraclePolicy(*[getattr(c, f) for f, _ in c._fields_])
+
+
+class OracleBackend:
+    """Casts and contractions on the oracle, for the checker's pass of the
+    training-step mirrors (drift_b200.mlp, drift_b200.attn)."""
+
+    name = "oracle"
+
+    def amax(self, x):
+        from oracle import oracle as O
+        return O.amax(x)
+
+    def per_tensor_scale(self, f, amax):
+        from oracle import oracle as O
+        return O.per_tensor_scale(f.id, amax)
+
+    def quantize(self, src, f, p, rm, scale, rng):
+        from oracle import oracle as O
+        st = rng.state() if rng is not None else None
+        dst, clamped, st = O.quantize(opolicy(p), f.id if f is not None else -1, int(rm), src,
+                                      scale, st)
+        if rng is not None:
+            rng.reseed(st)
+        return dst, clamped
+
+    def gemm(self, p, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks, bias=None, rng=None):
+        from oracle import oracle as O
+        st = rng.state() if rng is not None else None
+        C, st = O.gemm(opolicy(p), M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks,
+                       bias=bias, rng_state=st, threads=16)
+        if rng is not None:
+            rng.reseed(st)
+        return C
+
+    def contract(self, p, op, A, B, C, rng=None):
+        from oracle import oracle as O
+        st = O.contract(opolicy(p), op, A, B, C, rng.state() if rng is not None else None)
+        if rng is not None:
+            rng.reseed(st)
+        return C

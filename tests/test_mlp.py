@@ -4,40 +4,8 @@ against the same pass run on the oracle, gradients and Rng state included."""
 import numpy as np
 import pytest
 
+from helpers import OracleBackend
 from oracle import oracle as O
-
-
-class OracleBackend:
-    """Casts and contractions on the oracle, for the checker's pass."""
-
-    name = "oracle"
-
-    def amax(self, x):
-        return O.amax(x)
-
-    def per_tensor_scale(self, f, amax):
-        return O.per_tensor_scale(f.id, amax)
-
-    def quantize(self, src, f, p, rm, scale, rng):
-        pc = _opolicy(p)
-        st = rng.state() if rng is not None else None
-        dst, clamped, st = O.quantize(pc, f.id if f is not None else -1, int(rm), src, scale, st)
-        if rng is not None:
-            rng.reseed(st)
-        return dst, clamped
-
-    def gemm(self, p, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks, bias=None, rng=None):
-        st = rng.state() if rng is not None else None
-        C, st = O.gemm(_opolicy(p), M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks,
-                       bias=bias, rng_state=st, threads=16)
-        if rng is not None:
-            rng.reseed(st)
-        return C
-
-
-def _opolicy(p):
-    c = p.to_c()
-    return O.OraclePolicy(*[getattr(c, f) for f, _ in c._fields_])
 
 
 def test_host_pieces_without_gpu():
