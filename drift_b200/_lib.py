@@ -90,6 +90,12 @@ SIGNATURES = {
     "drift_error_sums_dev": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "drift_radix_hist_dev": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp]),
     "drift_radix_select_dev": (_int, [_vp, _int, _vp, _vp, _vp]),
+    "drift_embed_gather_dev": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp]),
+    "drift_embed_grad_dev": (_int, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp]),
+    "drift_bias_grad_dev": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    "drift_tanh_backward_dev": (_int, [_vp, _vp, _vp, _i64, _vp]),
+    "drift_scale_for_dev": (_int, [_vp, _int, _vp, _vp, _i32, _vp, _vp, _vp]),
+    "drift_adam_dev": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _d, _i32, _vp]),
     "drift_probe_fp64": (_int, [_vp, _P(_d)]),
     "drift_check_dev": (_int, [_vp, _vp]),
 }

@@ -171,6 +171,7 @@ static int take_device_error(drift_ctx *ctx, cudaStream_t st) {
     if (flags & DEV_ERR_NAN_FINITE) return fail(DRIFT_ENAN_FINITE, "NaN cast into a format without NaN");
     if (flags & DEV_ERR_NO_RNG) return fail(DRIFT_EINVAL, "stochastic rounding needs an Rng");
     if (flags & DEV_ERR_TIMEOUT) return fail(DRIFT_ETIMEOUT, "device wait gave up");
+    if (flags & DEV_ERR_INDEX) return fail(DRIFT_EINVAL, "token outside the embedding table");
     return DRIFT_OK;
 }
 
@@ -704,6 +705,77 @@ int drift_quantize_dev_noalloc(const drift_policy *p, int fmt, int rounding, con
     if (rc == DRIFT_ENOMEM)
         return fail(rc, "too many items for the fixed scratch array (DRIFT_NOALLOC_MAX_ITEMS)");
     return rc ? fail(rc, "no-allocation quantize launch") : DRIFT_OK;
+}
+
+// ------------------------------------------------------------------ training step
+
+int drift_embed_gather_dev(drift_ctx *ctx, const int32_t *d_tokens, int64_t n_tok,
+                           const double *d_table, int64_t vocab, int64_t width, double *d_out,
+                           void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n_tok < 0 || vocab < 0 || width < 0 || (n_tok * width > 0 && (!d_tokens || !d_table || !d_out)))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_embed_gather(d_tokens, n_tok, d_table, vocab, width, d_out, ctx->d_err(),
+                             pick(ctx, stream));
+    return rc ? fail(rc, "embedding gather") : DRIFT_OK;
+}
+
+int drift_embed_grad_dev(drift_ctx *ctx, const int32_t *d_tokens, int64_t n_tok,
+                         const double *d_rows, int64_t width, double *d_table_grad, int64_t vocab,
+                         void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n_tok < 0 || vocab < 0 || width < 0 ||
+        (n_tok * width * vocab > 0 && (!d_tokens || !d_rows || !d_table_grad)))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_embed_grad(d_tokens, n_tok, d_rows, width, d_table_grad, vocab, pick(ctx, stream));
+    return rc ? fail(rc, "embedding gradient") : DRIFT_OK;
+}
+
+int drift_bias_grad_dev(drift_ctx *ctx, const double *d_dy, int64_t rows, int64_t cols,
+                        double *d_db, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (rows < 0 || cols < 0 || (cols > 0 && (!d_db || (rows > 0 && !d_dy))))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_bias_grad(d_dy, rows, cols, d_db, pick(ctx, stream));
+    return rc ? fail(rc, "bias gradient") : DRIFT_OK;
+}
+
+int drift_tanh_backward_dev(drift_ctx *ctx, const double *d_out, double *d_grad, int64_t n,
+                            void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || (n > 0 && (!d_out || !d_grad))) return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_tanh_backward(d_out, d_grad, n, pick(ctx, stream));
+    return rc ? fail(rc, "tanh backward") : DRIFT_OK;
+}
+
+int drift_scale_for_dev(drift_ctx *ctx, int fmt, const double *d_amax_now, double *d_history,
+                        int32_t history_len, int64_t *d_count, double *d_scale, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!d_amax_now || !d_history || !d_count || !d_scale || history_len <= 0)
+        return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_scale_for(fmt, d_amax_now, d_history, history_len, d_count, d_scale,
+                          pick(ctx, stream));
+    return rc ? fail(rc, "delayed scale") : DRIFT_OK;
+}
+
+int drift_adam_dev(drift_ctx *ctx, double *d_param, const double *d_grad, double *d_m,
+                   double *d_v, int64_t n, int32_t step, double lr, int32_t fp32_master,
+                   void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (n < 0 || step < 1 || (n > 0 && (!d_param || !d_grad || !d_m || !d_v)))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    // Trainer.java:248-249, Math.pow on the host.
+    const double c1 = 1 - std::pow(0.9, (double)step);
+    const double c2 = 1 - std::pow(0.999, (double)step);
+    rc = launch_adam(d_param, d_grad, d_m, d_v, n, c1, c2, lr, fp32_master ? 1 : 0,
+                     pick(ctx, stream));
+    return rc ? fail(rc, "adam") : DRIFT_OK;
 }
 
 int drift_check_dev(drift_ctx *ctx, void *stream) {

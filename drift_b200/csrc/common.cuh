@@ -89,6 +89,11 @@ __host__ __device__ inline uint64_t draw_u53(uint64_t state, uint64_t k) {
 }
 
 // Device error flags, OR-ed into a context word and read by drift_check_dev.
-enum DevErr : int { DEV_ERR_NAN_FINITE = 1, DEV_ERR_NO_RNG = 2, DEV_ERR_TIMEOUT = 4 };
+enum DevErr : int {
+    DEV_ERR_NAN_FINITE = 1,
+    DEV_ERR_NO_RNG = 2,
+    DEV_ERR_TIMEOUT = 4,
+    DEV_ERR_INDEX = 8,  // a token outside the embedding table
+};
 
 }  // namespace drift

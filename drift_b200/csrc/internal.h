@@ -88,4 +88,16 @@ int launch_value_table(int fmt, uint64_t *d_bits, cudaStream_t st);
 int launch_pair_table(int fmt, int mode, uint64_t seed, int64_t first, int64_t n, int32_t *d_a,
                       int32_t *d_b, int32_t *d_prod, int32_t *d_sum, cudaStream_t st);
 
+// train.cu
+int launch_embed_gather(const int32_t *tokens, int64_t n_tok, const double *table, int64_t vocab,
+                        int64_t width, double *out, int *err, cudaStream_t st);
+int launch_embed_grad(const int32_t *tokens, int64_t n_tok, const double *rows, int64_t width,
+                      double *grad, int64_t vocab, cudaStream_t st);
+int launch_bias_grad(const double *dy, int64_t rows, int64_t cols, double *db, cudaStream_t st);
+int launch_tanh_backward(const double *out, double *grad, int64_t n, cudaStream_t st);
+int launch_scale_for(int fmt, const double *amax_now, double *hist, int32_t len, int64_t *count,
+                     double *scale, cudaStream_t st);
+int launch_adam(double *p, const double *g, double *m, double *v, int64_t n, double c1, double c2,
+                double lr, int fp32, cudaStream_t st);
+
 }  // namespace drift

@@ -117,19 +117,8 @@ class Pass:
         self.h2 = self._linear_forward(1, self.h1, n.hidden, n.w2, n.b2, n.hidden)
         self.h2 = np.tanh(self.h2)
         logits = self._linear_forward(2, self.h2, n.hidden, n.w3, n.b3, n.vocab).reshape(B, n.vocab)
-        # Softmax cross-entropy in double, summed in the Java order
-        # (Pass.java:134-153): z over k, then the loss over the batch.
-        mx = logits.max(axis=1, keepdims=True)
-        z = np.cumsum(np.exp(logits - mx), axis=1)[:, -1:]
-        log_z = np.log(z) + mx
-        rows = np.arange(B)
-        loss = 0.0
-        for i in range(B):
-            loss += float(log_z[i, 0] - logits[i, targets[i]])
-        d = np.exp(logits - log_z) / B
-        d[rows, targets] -= 1.0 / B
-        self.d_logits = d.reshape(-1)
-        return loss / B
+        loss, self.d_logits = softmax_xent(logits, targets)
+        return loss
 
     def loss_and_grads(self, contexts: np.ndarray, targets: np.ndarray) -> tuple:
         """Pass.lossAndGrads (Pass.java:108-113): loss and the gradients in
@@ -215,15 +204,33 @@ class Pass:
         return self.backend.per_tensor_scale(f, use)
 
 
+def softmax_xent(logits: np.ndarray, targets: np.ndarray):
+    """Softmax cross-entropy in double (Pass.java:134-153): z summed over k in
+    order, the loss over the batch in order. Returns the mean loss and the
+    flat gradient of the logits."""
+    B = logits.shape[0]
+    mx = logits.max(axis=1, keepdims=True)
+    z = np.cumsum(np.exp(logits - mx), axis=1)[:, -1:]
+    log_z = np.log(z) + mx
+    loss = 0.0
+    for i in range(B):
+        loss += float(log_z[i, 0] - logits[i, targets[i]])
+    d = np.exp(logits - log_z) / B
+    d[np.arange(B), targets] -= 1.0 / B
+    return loss / B, d.reshape(-1)
+
+
 def compare(got: List[np.ndarray], exact: List[np.ndarray]):
     """Trainer.compare (Trainer.java:272-288): cos, gain and rel over all
-    tensors concatenated."""
-    dot = gg = ee = dd = 0.0
-    for a, b in zip(got, exact):
-        dot += float(np.dot(a, b))
-        gg += float(np.dot(a, a))
-        ee += float(np.dot(b, b))
-        dd += float(np.dot(a - b, a - b))
+    tensors concatenated, each sum taken in order as the Java loop does."""
+    a = np.concatenate([np.asarray(x, dtype=np.float64).reshape(-1) for x in got])
+    b = np.concatenate([np.asarray(x, dtype=np.float64).reshape(-1) for x in exact])
+
+    def total(x):
+        return float(np.cumsum(x)[-1]) if x.size else 0.0
+
+    dot, gg, ee = total(a * b), total(a * a), total(b * b)
+    dd = total((a - b) * (a - b))
     return dot / np.sqrt(gg * ee), dot / ee, np.sqrt(dd / ee)
 
 

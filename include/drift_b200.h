@@ -359,6 +359,43 @@ DRIFT_API int drift_contract_dev(drift_ctx *ctx, const drift_policy *p,
                        const double *d_b, double *d_c, uint64_t *d_rng_state,
                        void *stream);
 
+/* ---------------------------------------- device-resident training step */
+/*
+ * The arithmetic of Pass/Trainer around the casts and contractions
+ * (java/.../train/Pass.java, Trainer.java), on device buffers, so a training
+ * step keeps its weights, casts, gradients and Adam moments on the GPU. Each
+ * keeps the Java loop order; results equal the host loops bit for bit.
+ */
+/* Pass.forward's lookup (Pass.java:122-126): out row r = table row
+ * tokens[r], rows of `width`. A token outside [0, vocab) is reported by
+ * drift_check_dev as DRIFT_EINVAL. */
+DRIFT_API int drift_embed_gather_dev(drift_ctx *ctx, const int32_t *d_tokens, int64_t n_tok,
+                           const double *d_table, int64_t vocab, int64_t width,
+                           double *d_out, void *stream);
+/* Pass.backward's embedding gradient (Pass.java:168-179): table_grad row v
+ * += rows[r] for every r with tokens[r] == v, in increasing r. */
+DRIFT_API int drift_embed_grad_dev(drift_ctx *ctx, const int32_t *d_tokens, int64_t n_tok,
+                         const double *d_rows, int64_t width, double *d_table_grad,
+                         int64_t vocab, void *stream);
+/* Pass.linearBackward's bias gradient (Pass.java:234-240): db[o] = the sum
+ * of dy[i*cols + o] over i in order. */
+DRIFT_API int drift_bias_grad_dev(drift_ctx *ctx, const double *d_dy, int64_t rows,
+                        int64_t cols, double *d_db, void *stream);
+/* Pass.tanhBackward (Pass.java:279-283): grad[i] *= 1 - out[i]^2. */
+DRIFT_API int drift_tanh_backward_dev(drift_ctx *ctx, const double *d_out, double *d_grad,
+                            int64_t n, void *stream);
+/* Pass.scaleFor with an amax history (Pass.java:249-271): the scale from the
+ * largest of the last min(count, len) amaxes (this step's when count is 0),
+ * then this step's amax recorded and *d_count advanced. */
+DRIFT_API int drift_scale_for_dev(drift_ctx *ctx, int fmt, const double *d_amax_now,
+                        double *d_history, int32_t history_len, int64_t *d_count,
+                        double *d_scale, void *stream);
+/* Trainer.adam for one tensor at `step` (1-based; Trainer.java:246-269),
+ * FP32 masters rounding weight and moments to float. */
+DRIFT_API int drift_adam_dev(drift_ctx *ctx, double *d_param, const double *d_grad,
+                   double *d_m, double *d_v, int64_t n, int32_t step, double lr,
+                   int32_t fp32_master, void *stream);
+
 /* No counterpart in the reference: measures the FP64 pipe's DMUL+DADD issue
  * rate on the context's device (operations per second), the denominator of
  * the contraction's roofline. Takes a few milliseconds. */
