@@ -480,6 +480,53 @@ def run_kernels(args):
     return 0
 
 
+def run_train(args):
+    """The training-step configuration (vocab 96, ctx 32, emb 64, hidden 2048,
+    batch 64) under fp8 delayed scaling with stochastic gradient rounding:
+    steps per second and emulated MAC/s of the device-resident step, and of
+    the same step through the host-buffer entry points. A step is one policy
+    pass and the Adam update; measurement steps (exact recompute) are moved
+    out of the timed window."""
+    import numpy as np
+    import torch
+    import drift_b200 as d
+    from drift_b200 import mlp, mlp_dev
+
+    p = (d.policies.by_name("fp8-delayed").to_builder("fp8-delayed-sr-grads")
+         .grad_rounding(d.Rounding.STOCHASTIC).build())
+    far = 10 ** 9   # no measurement step inside the timed window
+    tr = mlp_dev.DeviceTrainer(p, 0, measure_every=far)
+    for _ in range(args.warmup):
+        tr.step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tr.step()
+    torch.cuda.synchronize()
+    dev_s = (time.perf_counter() - t0) / args.steps
+    tr.result()
+    macs = tr.macs_per_step()
+
+    net = mlp.Net(96, 32, 64, 2048, 1000)
+    net.round_to_fp32()
+    pas = mlp.Pass(p, net, 64, 0xC0FFEE)
+    rs = np.random.default_rng(0)
+    ctx, tgt = rs.integers(0, 96, 64 * 32), rs.integers(0, 96, 64)
+    pas.loss_and_grads(ctx, tgt)
+    t0 = time.perf_counter()
+    n_host = max(1, min(args.steps, 3))
+    for _ in range(n_host):
+        pas.loss_and_grads(ctx, tgt)
+    host_s = (time.perf_counter() - t0) / n_host
+    print(json.dumps({"mode": "train", "policy": p.name, "macs_per_step": macs,
+                      "config": {"vocab": 96, "ctx": 32, "emb": 64, "hidden": 2048, "batch": 64},
+                      "device_resident": {"s_per_step": dev_s, "mac_per_s": macs / dev_s,
+                                          "steps": args.steps},
+                      "host_buffers": {"s_per_step": host_s, "mac_per_s": macs / host_s,
+                                       "steps": n_host, "note": "no Adam step"}}), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -491,7 +538,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
-    ap.add_argument("--mode", choices=["sweep", "kernels"], default="sweep",
+    ap.add_argument("--mode", choices=["sweep", "kernels", "train"], default="sweep",
                     help="kernels: time each policy's contraction alone (for profiling)")
     ap.add_argument("--policies", default="", help="kernels mode: comma-separated policy names")
     args = ap.parse_args()
@@ -501,6 +548,8 @@ def main() -> int:
         return run_reference(args)
     if args.mode == "kernels":
         return run_kernels(args)
+    if args.mode == "train":
+        return run_train(args)
     return run_engine(args)
 
 

@@ -132,9 +132,16 @@ void ScheduleCache::clear() {
 
 // ------------------------------------------------------------------ context
 
+constexpr int kPipeChunks = 8;  // host-buffer calls copy and compute in up to 8 chunks
+
 struct drift_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
+    // Copy streams and events of the pipelined host-buffer calls: chunk c
+    // goes in on `h2d`, is computed on `stream`, and comes back on `d2h`.
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t ev_in[kPipeChunks] = {}, ev_done[kPipeChunks] = {};
+    cudaEvent_t ev_start = nullptr;
     Workspace ws;       // kernel scratch
     Workspace io;       // staging for host-buffer calls
     ScheduleCache sched;
@@ -175,6 +182,42 @@ static int take_device_error(drift_ctx *ctx, cudaStream_t st) {
     return DRIFT_OK;
 }
 
+// ------------------------------------------------------------------ pipelines
+//
+// A host-buffer call moves its operands over PCIe at about 55 GB/s each way.
+// Large calls split into up to kPipeChunks chunks: chunk c is copied in on
+// ctx->h2d, computed on ctx->stream once its copy has landed, and copied out
+// on ctx->d2h once computed, so the copies of one chunk overlap the compute
+// of its neighbours. Every pipelined call waits for both copy streams before
+// it returns, on every path, so the staging buffer is never reused early.
+
+// The copy streams start after everything already queued on ctx->stream
+// (the staging buffer's stream-ordered allocation included).
+static int pipe_begin(drift_ctx *ctx) {
+    CUDA_TRY(cudaEventRecord(ctx->ev_start, ctx->stream), "record");
+    CUDA_TRY(cudaStreamWaitEvent(ctx->h2d, ctx->ev_start, 0), "wait");
+    CUDA_TRY(cudaStreamWaitEvent(ctx->d2h, ctx->ev_start, 0), "wait");
+    return DRIFT_OK;
+}
+
+// Waits for both copy streams; returns `rc` unless waiting itself failed.
+static int pipe_end(drift_ctx *ctx, int rc) {
+    const cudaError_t a = cudaStreamSynchronize(ctx->h2d);
+    const cudaError_t b = cudaStreamSynchronize(ctx->d2h);
+    if (rc) return rc;
+    if (a != cudaSuccess) return cuda_fail(a, "synchronize");
+    if (b != cudaSuccess) return cuda_fail(b, "synchronize");
+    return DRIFT_OK;
+}
+
+// Chunk length in units of `unit` elements (or rows) for a call of n of
+// them; 0 when the call is too small to gain from a pipeline.
+static int64_t pipe_chunk(int64_t n, int64_t min_total, int64_t unit) {
+    if (n < min_total) return 0;
+    int64_t c = (n + kPipeChunks - 1) / kPipeChunks;
+    return (c + unit - 1) / unit * unit;
+}
+
 extern "C" {
 
 const char *drift_last_error(void) { return g_last_error.c_str(); }
@@ -191,9 +234,23 @@ int drift_open(int device, drift_ctx **out) {
     drift_ctx *ctx = new drift_ctx();
     ctx->device = device;
     cudaError_t e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->h2d, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->d2h, cudaStreamNonBlocking);
+    for (int c = 0; c < kPipeChunks && e == cudaSuccess; c++) {
+        e = cudaEventCreateWithFlags(&ctx->ev_in[c], cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_done[c], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_start, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_small, 64);
     if (e == cudaSuccess) e = cudaMemset(ctx->d_small, 0, 64);
     if (e != cudaSuccess) {
+        for (int c = 0; c < kPipeChunks; c++) {
+            if (ctx->ev_in[c]) cudaEventDestroy(ctx->ev_in[c]);
+            if (ctx->ev_done[c]) cudaEventDestroy(ctx->ev_done[c]);
+        }
+        if (ctx->ev_start) cudaEventDestroy(ctx->ev_start);
+        if (ctx->h2d) cudaStreamDestroy(ctx->h2d);
+        if (ctx->d2h) cudaStreamDestroy(ctx->d2h);
         if (ctx->stream) cudaStreamDestroy(ctx->stream);
         delete ctx;
         return cuda_fail(e, "drift_open");
@@ -211,6 +268,13 @@ int drift_close(drift_ctx *ctx) {
     cudaStreamSynchronize(ctx->stream);
     ctx->sched.clear();
     cudaFree(ctx->d_small);
+    for (int c = 0; c < kPipeChunks; c++) {
+        cudaEventDestroy(ctx->ev_in[c]);
+        cudaEventDestroy(ctx->ev_done[c]);
+    }
+    cudaEventDestroy(ctx->ev_start);
+    cudaStreamDestroy(ctx->h2d);
+    cudaStreamDestroy(ctx->d2h);
     cudaStreamDestroy(ctx->stream);
     delete ctx;
     return DRIFT_OK;
@@ -399,8 +463,48 @@ int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt, int rounding,
     if (!buf) return fail(DRIFT_ENOMEM, "staging");
     double *d_src = (double *)buf;
     double *d_dst = (double *)(buf + n * 8);
-    CUDA_TRY(cudaMemcpyAsync(d_src, src, n * 8, cudaMemcpyHostToDevice, st), "copy in");
     CUDA_TRY(cudaMemsetAsync(ctx->d_clamped(), 0, 8, st), "clear clamps");
+    // Without stochastic rounding the elements (and MX blocks, which follow
+    // the flat index from 0) are independent, so the cast travels in chunks
+    // whose copies overlap: in on one copy engine, out on the other.
+    const int64_t unit = (p->scaling == DRIFT_MX_BLOCK && p->scale_block > 0 ? p->scale_block : 1) * 256;
+    const int64_t chunk = rounding != DRIFT_STOCHASTIC ? pipe_chunk(n, (int64_t)1 << 22, unit) : 0;
+    if (chunk > 0) {
+        rc = pipe_begin(ctx);
+        int c = 0;
+        for (int64_t e0 = 0; e0 < n && !rc; e0 += chunk, c++) {
+            const int64_t len = n - e0 < chunk ? n - e0 : chunk;
+            if (cudaMemcpyAsync(d_src + e0, src + e0, len * 8, cudaMemcpyHostToDevice, ctx->h2d) !=
+                    cudaSuccess ||
+                cudaEventRecord(ctx->ev_in[c], ctx->h2d) != cudaSuccess ||
+                cudaStreamWaitEvent(st, ctx->ev_in[c], 0) != cudaSuccess) {
+                rc = fail(DRIFT_ECUDA, "copy in");
+                break;
+            }
+            rc = launch_quantize(ctx->ws, p, fmt, rounding, d_src + e0, d_dst + e0, len, nullptr,
+                                 scale, nullptr, ctx->d_clamped(), ctx->d_err(), st);
+            if (rc) {
+                rc = fail(rc, "quantize launch");
+                break;
+            }
+            if (cudaEventRecord(ctx->ev_done[c], st) != cudaSuccess ||
+                cudaStreamWaitEvent(ctx->d2h, ctx->ev_done[c], 0) != cudaSuccess ||
+                cudaMemcpyAsync(dst + e0, d_dst + e0, len * 8, cudaMemcpyDeviceToHost, ctx->d2h) !=
+                    cudaSuccess)
+                rc = fail(DRIFT_ECUDA, "copy out");
+        }
+        unsigned long long clamped = 0;
+        if (!rc && cudaMemcpyAsync(&clamped, ctx->d_clamped(), 8, cudaMemcpyDeviceToHost, st) !=
+                       cudaSuccess)
+            rc = fail(DRIFT_ECUDA, "clamps out");
+        rc = pipe_end(ctx, rc);
+        if (rc) return rc;
+        rc = take_device_error(ctx, st);
+        if (rc) return rc;
+        if (clamped_out) *clamped_out = (int64_t)clamped;
+        return DRIFT_OK;
+    }
+    CUDA_TRY(cudaMemcpyAsync(d_src, src, n * 8, cudaMemcpyHostToDevice, st), "copy in");
     if (rng_state)
         CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), rng_state, 8, cudaMemcpyHostToDevice, st), "rng in");
     rc = launch_quantize(ctx->ws, p, fmt, rounding, d_src, d_dst, n, nullptr, scale,
@@ -477,10 +581,43 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
     double *d_b = d_a + ((sa + 1) & ~1LL);
     double *d_c = d_b + ((sb + 1) & ~1LL);
     double *d_bias = bias ? d_c + ((sc + 1) & ~1LL) : nullptr;
-    if (sa) CUDA_TRY(cudaMemcpyAsync(d_a, A + a_off, sa * 8, cudaMemcpyHostToDevice, st), "copy A");
+    const bool sr = stochastic_acc(p);
+    // Rows of a row-major A own disjoint spans, so A can travel in row chunks
+    // (multiples of the 64-row tile) that overlap the contraction.
+    const int64_t chunk = (!sr && K > 0 && a_k_stride == 1 && a_row_stride >= K)
+                              ? pipe_chunk(M, 1024, 64) : 0;
     if (sb) CUDA_TRY(cudaMemcpyAsync(d_b, B + b_off, sb * 8, cudaMemcpyHostToDevice, st), "copy B");
     if (bias) CUDA_TRY(cudaMemcpyAsync(d_bias, bias, N * 8, cudaMemcpyHostToDevice, st), "copy bias");
-    const bool sr = stochastic_acc(p);
+    if (chunk > 0) {
+        rc = pipe_begin(ctx);
+        int c = 0;
+        for (int64_t r0 = 0; r0 < M && !rc; r0 += chunk, c++) {
+            const int64_t rows = M - r0 < chunk ? M - r0 : chunk;
+            const int64_t off = r0 * a_row_stride;
+            if (cudaMemcpyAsync(d_a + off, A + a_off + off, span_of(rows, a_row_stride, K, 1) * 8,
+                                cudaMemcpyHostToDevice, ctx->h2d) != cudaSuccess ||
+                cudaEventRecord(ctx->ev_in[c], ctx->h2d) != cudaSuccess ||
+                cudaStreamWaitEvent(st, ctx->ev_in[c], 0) != cudaSuccess) {
+                rc = fail(DRIFT_ECUDA, "copy A");
+                break;
+            }
+            rc = launch_gemm(ctx->ws, ctx->sched, p, rows, N, K, d_a + off, a_row_stride, 1, d_b,
+                             b_row_stride, b_k_stride, d_bias, d_c + r0 * N, N, ctx->d_err(), st);
+            if (rc) {
+                rc = fail(rc, "gemm launch");
+                break;
+            }
+            if (cudaEventRecord(ctx->ev_done[c], st) != cudaSuccess ||
+                cudaStreamWaitEvent(ctx->d2h, ctx->ev_done[c], 0) != cudaSuccess ||
+                cudaMemcpy2DAsync(C + r0 * c_row_stride, c_row_stride * 8, d_c + r0 * N, N * 8,
+                                  N * 8, rows, cudaMemcpyDeviceToHost, ctx->d2h) != cudaSuccess)
+                rc = fail(DRIFT_ECUDA, "copy C");
+        }
+        rc = pipe_end(ctx, rc);
+        if (rc) return rc;
+        return take_device_error(ctx, st);
+    }
+    if (sa) CUDA_TRY(cudaMemcpyAsync(d_a, A + a_off, sa * 8, cudaMemcpyHostToDevice, st), "copy A");
     if (sr) {
         // The Rng state travels on the device; without one, start from zero
         // and fail afterwards if any draw was taken (Java fails on the first).

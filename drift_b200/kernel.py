@@ -200,7 +200,11 @@ class Quant:
         overload does."""
         rm = p.input_rounding if rm is None else Rounding(rm)
         s = np.ascontiguousarray(np.asarray(src, dtype=np.float64).reshape(-1)[src_off:src_off + n])
-        out = np.empty(n, dtype=np.float64)
+        # The engine writes into dst itself when dst is contiguous float64
+        # (no temporary, no second host copy).
+        direct = (isinstance(dst, np.ndarray) and dst.dtype == np.float64
+                  and dst.flags.c_contiguous)
+        out = dst.reshape(-1)[dst_off:dst_off + n] if direct else np.empty(n, dtype=np.float64)
         st = _state_in(rng)
         clamped = ctypes.c_int64()
         pc = p.to_c()
@@ -209,7 +213,8 @@ class Quant:
             int(rm), s.ctypes.data, out.ctypes.data, n, float(scale),
             ctypes.byref(st) if st is not None else None, ctypes.byref(clamped)))
         _state_out(rng, st)
-        dst.reshape(-1)[dst_off:dst_off + n] = out
+        if not direct:
+            dst.reshape(-1)[dst_off:dst_off + n] = out
         return int(clamped.value)
 
 

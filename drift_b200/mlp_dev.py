@@ -175,47 +175,78 @@ def _signed(x: int) -> int:
     return x - (1 << 64) if x >> 63 else x
 
 
-def train(policy: NumericPolicy, seed: int, *, vocab=96, ctx=32, emb=64, hidden=2048, batch=64,
-          steps=25, measure_every=25, lr=1e-3, device: int = 0) -> Dict:
-    """drift_b200.mlp.train with the state on GPU `device`: the same token
-    stream, Rng seeds, measurement schedule and records."""
-    import torch
+class DeviceTrainer:
+    """Trainer.run's step (Trainer.java:78-205) with the state on GPU
+    `device`: the same token stream, Rng seeds, measurement schedule and
+    records as drift_b200.mlp.train."""
 
-    dev = torch.device("cuda", device)
-    _lib.Context.use_device(device)
-    net = Net(vocab, ctx, emb, hidden, 1000 + seed)
-    if policy.master_fp32:
-        net.round_to_fp32()
-    params = [torch.from_numpy(t.copy()).to(dev) for t in net.tensors()]
-    m = [torch.zeros_like(t) for t in params]
-    v = [torch.zeros_like(t) for t in params]
-    pas = DevicePass(policy, net, params, batch, 0xC0FFEE * (seed + 1), dev)
-    exact = DevicePass(NumericPolicy.exact(), net, params, batch, 1, dev)
-    tokens = np.random.default_rng(seed)
-    records: List[StepRecord] = []
-    st = _stream_ptr()
-    for step in range(1, steps + 1):
-        contexts = tokens.integers(0, vocab, size=batch * ctx)
-        targets = tokens.integers(0, vocab, size=batch)
-        d_ctx = torch.from_numpy(contexts.astype(np.int32)).to(dev)
-        loss = pas.loss_and_grads(d_ctx, targets)
-        rec = StepRecord(step, loss)
-        if step % measure_every == 0 or step == 1:
-            rec.loss_exact = exact.loss_and_grads(d_ctx, targets)
+    def __init__(self, policy: NumericPolicy, seed: int, *, vocab=96, ctx=32, emb=64, hidden=2048,
+                 batch=64, measure_every=25, lr=1e-3, device: int = 0):
+        import torch
+
+        self.torch = torch
+        self.policy = policy
+        self.dev = torch.device("cuda", device)
+        _lib.Context.use_device(device)
+        self.vocab, self.ctx, self.batch = vocab, ctx, batch
+        self.measure_every, self.lr = measure_every, float(lr)
+        net = Net(vocab, ctx, emb, hidden, 1000 + seed)
+        if policy.master_fp32:
+            net.round_to_fp32()
+        self.net = net
+        self.params = [torch.from_numpy(t.copy()).to(self.dev) for t in net.tensors()]
+        self.m = [torch.zeros_like(t) for t in self.params]
+        self.v = [torch.zeros_like(t) for t in self.params]
+        self.pas = DevicePass(policy, net, self.params, batch, 0xC0FFEE * (seed + 1), self.dev)
+        self.exact = DevicePass(NumericPolicy.exact(), net, self.params, batch, 1, self.dev)
+        self.tokens = np.random.default_rng(seed)
+        self.step_no = 0
+        self.records: List[StepRecord] = []
+
+    def macs_per_step(self) -> int:
+        """Emulated MACs of one policy pass: forward, dgrad and wgrad of the
+        three linears (the exact recompute at measurement steps excluded)."""
+        n = self.net
+        fwd = self.batch * (n.in1 * n.hidden + n.hidden * n.hidden + n.hidden * n.vocab)
+        return 3 * fwd
+
+    def step(self) -> StepRecord:
+        torch = self.torch
+        self.step_no += 1
+        step = self.step_no
+        contexts = self.tokens.integers(0, self.vocab, size=self.batch * self.ctx)
+        targets = self.tokens.integers(0, self.vocab, size=self.batch)
+        d_ctx = torch.from_numpy(contexts.astype(np.int32)).to(self.dev)
+        pas = self.pas
+        rec = StepRecord(step, pas.loss_and_grads(d_ctx, targets))
+        if step % self.measure_every == 0 or step == 1:
+            rec.loss_exact = self.exact.loss_and_grads(d_ctx, targets)
             rec.cos, rec.gain, rec.rel = compare([g.cpu().numpy() for g in pas.grads],
-                                                 [g.cpu().numpy() for g in exact.grads])
+                                                 [g.cpu().numpy() for g in self.exact.grads])
             cl = pas.clamped.cpu().numpy()
             c = pas.cast
             rec.clamp_x = cl[T_X] / c[T_X] if c[T_X] else 0.0
             rec.clamp_w = cl[T_W] / c[T_W] if c[T_W] else 0.0
             rec.clamp_g = cl[T_G] / c[T_G] if c[T_G] else 0.0
-        records.append(rec)
-        for p_, g_, m_, v_ in zip(params, pas.grads, m, v):
+        self.records.append(rec)
+        st = _stream_ptr()
+        for p_, g_, m_, v_ in zip(self.params, pas.grads, self.m, self.v):
             _call("drift_adam_dev", _tptr(p_), _tptr(g_), _tptr(m_), _tptr(v_), p_.numel(), step,
-                  float(lr), int(policy.master_fp32), st)
-    pas.check()
-    torch.cuda.synchronize()
-    state = int(pas.state.item()) & 0xFFFFFFFFFFFFFFFF
-    return {"records": records, "rng_state": state,
-            "grads": [g.cpu().numpy() for g in pas.grads],
-            "params": [p_.cpu().numpy() for p_ in params]}
+                  self.lr, int(self.policy.master_fp32), st)
+        return rec
+
+    def result(self) -> Dict:
+        self.pas.check()
+        self.torch.cuda.synchronize()
+        state = int(self.pas.state.item()) & 0xFFFFFFFFFFFFFFFF
+        return {"records": self.records, "rng_state": state,
+                "grads": [g.cpu().numpy() for g in self.pas.grads],
+                "params": [p_.cpu().numpy() for p_ in self.params]}
+
+
+def train(policy: NumericPolicy, seed: int, *, steps=25, **kw) -> Dict:
+    """drift_b200.mlp.train with the state on the GPU (keyword `device`)."""
+    t = DeviceTrainer(policy, seed, **kw)
+    for _ in range(steps):
+        t.step()
+    return t.result()
