@@ -518,7 +518,45 @@ def run_train(args):
     for _ in range(n_host):
         pas.loss_and_grads(ctx, tgt)
     host_s = (time.perf_counter() - t0) / n_host
+    # The four attention contractions of AttnPass (scores, context, dProb, dv)
+    # at batch 64, t 256, d 64, device-resident; MACs count the dots actually
+    # taken (the causal half of scores and dProb, the ragged windows).
+    Bt, T, D = 64, 256, 64
+    W = d.Window
+    ops = {
+        "scores": (d.contraction(batch=Bt, rows=T, cols=T, depth=D, a_batch=T * D, a_row=D, a_k=1,
+                                 b_batch=T * D, b_col=D, b_k=1, c_batch=T * T, c_row=T,
+                                 alpha=0.125, causal=True), T * D, T * D, T * T,
+                   T * (T + 1) // 2 * D),
+        "context": (d.contraction(batch=Bt, rows=T, cols=D, depth=T, a_batch=T * T, a_row=T, a_k=1,
+                                  b_batch=T * D, b_col=1, b_k=D, c_batch=T * D, c_row=D,
+                                  window=W.PREFIX), T * T, T * D, T * D, T * (T + 1) // 2 * D),
+        "dv": (d.contraction(batch=Bt, rows=T, cols=D, depth=T, a_batch=T * T, a_row=1, a_k=T,
+                             b_batch=T * D, b_col=1, b_k=D, c_batch=T * D, c_row=D,
+                             window=W.SUFFIX), T * T, T * D, T * D, T * (T + 1) // 2 * D),
+    }
+    attn = {}
+    dev = torch.device("cuda", 0)
+    for pname in ("exact", "fp8-acc-bf16", "acc-bf16-pairwise"):
+        pol = d.policies.by_name(pname)
+        row = {}
+        for name, (op, na, nb, nc, macs_b) in ops.items():
+            A = torch.randn(Bt * na, dtype=torch.float64, device=dev)
+            Bm = torch.randn(Bt * nb, dtype=torch.float64, device=dev)
+            C = torch.empty(Bt * nc, dtype=torch.float64, device=dev)
+            d.contract_dev(pol, op, A, Bm, C)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                d.contract_dev(pol, op, A, Bm, C)
+            e1.record()
+            torch.cuda.synchronize()
+            row[name] = Bt * macs_b * args.steps / (e0.elapsed_time(e1) * 1e-3)
+        attn[pname] = row
+    d.check_dev()
+
     print(json.dumps({"mode": "train", "policy": p.name, "macs_per_step": macs,
+                      "attention_mac_per_s": attn,
                       "config": {"vocab": 96, "ctx": 32, "emb": 64, "hidden": 2048, "batch": 64},
                       "device_resident": {"s_per_step": dev_s, "mac_per_s": macs / dev_s,
                                           "steps": args.steps},

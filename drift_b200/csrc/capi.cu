@@ -623,10 +623,10 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
         // and fail afterwards if any draw was taken (Java fails on the first).
         const uint64_t s0 = rng_state ? *rng_state : 0;
         CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), &s0, 8, cudaMemcpyHostToDevice, st), "rng in");
-        rc = launch_contract(ctx->ws, p,
+        rc = launch_contract(ctx->ws, ctx->sched, p,
                              gemm_as_contraction(M, N, K, d_a, a_row_stride, a_k_stride, d_b,
                                                  b_row_stride, b_k_stride, d_bias, d_c, N),
-                             ctx->d_state(), st);
+                             ctx->d_state(), ctx->d_err(), st);
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
                          b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), st);
@@ -694,11 +694,11 @@ int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, 
     if (M > 0 && N > 0 && (!d_C || (K > 0 && (!d_A || !d_B)))) return fail(DRIFT_EINVAL, "null buffer");
     if (stochastic_acc(p)) {
         if (!d_rng_state) return fail(DRIFT_EINVAL, "stochastic accumulation needs d_rng_state");
-        rc = launch_contract(ctx->ws, p,
+        rc = launch_contract(ctx->ws, ctx->sched, p,
                              gemm_as_contraction(M, N, K, d_A, a_row_stride, a_k_stride, d_B,
                                                  b_row_stride, b_k_stride, d_bias, d_C,
                                                  c_row_stride),
-                             d_rng_state, pick(ctx, stream));
+                             d_rng_state, ctx->d_err(), pick(ctx, stream));
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
                          b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->d_err(),
@@ -770,7 +770,8 @@ int drift_contract(drift_ctx *ctx, const drift_policy *p, const drift_contractio
         CUDA_TRY(cudaMemcpyAsync(ctx->d_state(), &s0, 8, cudaMemcpyHostToDevice, st), "rng in");
     }
     ContractDesc d{*op, d_a, d_b, d_c, nullptr};
-    rc = launch_contract(ctx->ws, p, d, sr ? ctx->d_state() : nullptr, st);
+    rc = launch_contract(ctx->ws, ctx->sched, p, d, sr ? ctx->d_state() : nullptr, ctx->d_err(),
+                         st);
     if (rc) return fail(rc, "contraction launch");
     CUDA_TRY(cudaMemcpyAsync(c, d_c, c_len * 8, cudaMemcpyDeviceToHost, st), "copy C");
     uint64_t s1 = 0;
@@ -797,7 +798,7 @@ int drift_contract_dev(drift_ctx *ctx, const drift_policy *p, const drift_contra
     if (stochastic_acc(p) && !d_rng_state)
         return fail(DRIFT_EINVAL, "stochastic accumulation needs d_rng_state");
     ContractDesc d{*op, d_a, d_b, d_c, nullptr};
-    rc = launch_contract(ctx->ws, p, d, d_rng_state, pick(ctx, stream));
+    rc = launch_contract(ctx->ws, ctx->sched, p, d, d_rng_state, ctx->d_err(), pick(ctx, stream));
     return rc ? fail(rc, "contraction launch") : DRIFT_OK;
 }
 

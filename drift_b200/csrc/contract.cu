@@ -437,8 +437,34 @@ static bool stochastic(const drift_policy *p) {
            (p->acc == DRIFT_ACC_FP16 || p->acc == DRIFT_ACC_BF16);
 }
 
-int launch_contract(Workspace &ws, const drift_policy *p, const ContractDesc &d, uint64_t *d_state,
-                    cudaStream_t st) {
+// The score scale and the causal mask over a contraction the tiled kernel
+// computed whole: masked outputs become 0.0, the others dot * alpha.
+__global__ void contract_epilogue_kernel(const ContractArgs g) {
+    const int64_t total = g.batch * g.rows * g.cols;
+    for (int64_t out = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; out < total;
+         out += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t o = out % g.cols, i = (out / g.cols) % g.rows, t = out / g.cols / g.rows;
+        double *c = g.C + t * g.c_batch + i * g.c_row + o * g.c_col;
+        if (g.causal && o > i) *c = 0.0;
+        else if (g.alpha != 1.0) *c = __dmul_rn(*c, g.alpha);
+    }
+}
+
+// A FULL-window contraction that writes (not adds) rows of C with unit
+// column stride is a batch of plain contractions: the tiled TMA kernel of
+// gemm.cu takes it, the causal upper triangle included (each output's dot is
+// the same computation either way), and the epilogue then clears the masked
+// outputs and applies the scale.
+static bool tiled_route(const ContractDesc &d) {
+    const drift_contraction &op = d.op;
+    return op.window == DRIFT_WINDOW_FULL && !op.accumulate && op.c_col == 1 && !d.bias &&
+           op.batch <= 65535 && (op.rows + 63) / 64 <= 65535 && op.c_row >= op.cols &&
+           op.a_batch >= 0 && op.a_row >= 0 && op.a_k >= 0 && op.b_batch >= 0 && op.b_col >= 0 &&
+           op.b_k >= 0 && op.c_batch >= 0;
+}
+
+int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
+                    const ContractDesc &d, uint64_t *d_state, int *d_err, cudaStream_t st) {
     int rc = check_contraction(d.op);
     if (rc) return rc;
     const int64_t total = d.op.batch * d.op.rows * d.op.cols;
@@ -449,6 +475,15 @@ int launch_contract(Workspace &ws, const drift_policy *p, const ContractDesc &d,
     ContractArgs g = args_of(p, d);
     const unsigned grid = grid_of(total);
 
+    if (!stochastic(p) && tiled_route(d)) {
+        const drift_contraction &op = d.op;
+        rc = launch_gemm_batched(ws, cache, p, op.batch, op.rows, op.cols, op.depth, g.A, op.a_row,
+                                 op.a_k, op.a_batch, g.B, op.b_col, op.b_k, op.b_batch, nullptr,
+                                 g.C, op.c_row, op.c_batch, d_err, st);
+        if (rc) return rc;
+        if (op.causal || op.alpha != 1.0) contract_epilogue_kernel<<<grid, 128, 0, st>>>(g);
+        return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+    }
     if (!stochastic(p)) {
         const bool tr = p->acc_rounding == DRIFT_TRUNCATE;
         switch (p->acc) {

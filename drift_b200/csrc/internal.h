@@ -75,8 +75,15 @@ struct ContractDesc {
     const double *bias;
 };
 int check_contraction(const drift_contraction &op);
-int launch_contract(Workspace &ws, const drift_policy *p, const ContractDesc &d, uint64_t *d_state,
-                    cudaStream_t st);
+int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
+                    const ContractDesc &d, uint64_t *d_state, int *d_err, cudaStream_t st);
+// A batch of `batch` contractions, problem z at A + z*a_bs, B + z*b_bs,
+// C + z*c_bs (element strides), all with the same shape and bias.
+int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t batch,
+                        int64_t M, int64_t N, int64_t K, const double *A, int64_t a_rs,
+                        int64_t a_ks, int64_t a_bs, const double *B, int64_t b_rs, int64_t b_ks,
+                        int64_t b_bs, const double *bias, double *C, int64_t c_rs, int64_t c_bs,
+                        int *d_err, cudaStream_t st);
 int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,

@@ -145,3 +145,18 @@ def test_bad_contractions_are_rejected(d):
     op.window = 7
     with pytest.raises(d.DriftError):
         d.contract(p, op, A, Bm, np.zeros(9))
+
+
+@pytest.mark.parametrize("acc,order", [(a, o) for a in range(4) for o in range(4)])
+def test_full_windows_through_the_tiled_kernel(d, acc, order):
+    """Scores and dProb with an even depth: the batch runs as one tiled TMA
+    launch whose tiles read past each problem's last row into the next
+    problem (t = 70 is not a multiple of the 64-row tile), then the causal
+    mask and the score scale are applied."""
+    rs = np.random.default_rng(31 * acc + order)
+    p = d.NumericPolicy.builder("c").acc(d.Acc(acc)).order(d.Order(order)).acc_block(16).build()
+    for B, t, dim in [(3, 70, 16), (2, 128, 64), (5, 33, 40)]:
+        for name, op, na, nb, nc in attention_ops(d, B, t, dim, 0.3)[::2]:   # scores, dprob
+            got, want, _, _ = run(d, p, op, heavy_tailed(rs, na), heavy_tailed(rs, nb),
+                                  np.full(nc, 3.0))
+            assert_bits(got, want, f"{name} B={B} t={t} d={dim}")
