@@ -99,7 +99,13 @@ __device__ __forceinline__ double sr_round(double x, uint64_t state, uint64_t id
 // The accumulator's rounding after each add (Dot.java:43-63): identity for
 // FP64, (float) for FP32, Dot.round for FP16/BF16.
 template <int ACC, int RM> struct ExactRounder {
-    __device__ double operator()(double t) { return AccRound<ACC, RM>::exact(t); }
+    __device__ double operator()(double t) {
+        // The contraction kernel's fast rounding, checked; the exact form
+        // only when the result leaves the accumulator's normal range.
+        using R = AccRound<ACC, RM>;
+        const double r = R::fast(t);
+        return R::ok(r) ? r : R::exact(t);
+    }
 };
 
 template <int ACC> struct SrRounder {
