@@ -47,6 +47,7 @@
 // so control flow is uniform across the CTA.
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 #include <cuda.h>
@@ -143,7 +144,9 @@ __device__ __forceinline__ void round16(double (&t)[TM][TN]) {
 
 // One k step for the thread's 16 outputs: acc = round(acc + a_i * b_j), the
 // rounded value written straight into the accumulator.
-template <int ACC, int RM, int G = GROUP_ROWS>
+// FIRST starts a fresh sum: acc = round(0.0 + a_i * b_j), whatever acc held
+// (0.0 + p is not p when p is -0.0, so the add stays).
+template <int ACC, int RM, int G = GROUP_ROWS, bool FIRST = false>
 __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[TM],
                                       const double (&b)[TN]) {
     using R = AccRound<ACC, RM>;
@@ -151,7 +154,8 @@ __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[T
 #pragma unroll
         for (int i = 0; i < TM; i++)
 #pragma unroll
-            for (int j = 0; j < TN; j++) acc[i][j] = __dadd_rn(acc[i][j], __dmul_rn(a[i], b[j]));
+            for (int j = 0; j < TN; j++)
+                acc[i][j] = __dadd_rn(FIRST ? 0.0 : acc[i][j], __dmul_rn(a[i], b[j]));
     } else {
 #pragma unroll
         for (int i0 = 0; i0 < TM; i0 += G) {
@@ -161,7 +165,7 @@ __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[T
             for (int i = 0; i < G; i++)
 #pragma unroll
                 for (int j = 0; j < TN; j++) {
-                    t[i][j] = __dadd_rn(acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j]));
+                    t[i][j] = __dadd_rn(FIRST ? 0.0 : acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j]));
                     acc[i0 + i][j] = R::fast(t[i][j]);
                     ok = ok & R::ok(acc[i0 + i][j]);
                 }
@@ -321,7 +325,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
         }
     };
 
-    auto push = [&](int merges) {
+    // `fresh`: the next leaf starts with a FIRST step, so acc need not be zeroed.
+    auto push = [&](int merges, bool fresh = false) {
         for (; merges > 0; merges--) {
             sp--;
             combine<ACC, RM>(stk[sp], acc);
@@ -331,7 +336,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
 #pragma unroll
             for (int j = 0; j < TN; j++) {
                 stk[sp][i][j] = acc[i][j];
-                acc[i][j] = 0.0;
+                if (!fresh) acc[i][j] = 0.0;
             }
         sp++;
     };
@@ -380,10 +385,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
 
         if (SEG != SEG_SCHED && kn == BK) {
             // A full tile, no per-k segment work: two k per 16-byte read.
-            double leaf0[PAIR ? TM : 1][PAIR ? TN : 1];
-            constexpr int kUnroll = kp_unroll<ACC, ORDER>();
-#pragma unroll kUnroll
-            for (int q = 0; q < BK / 2; q++) {
+            constexpr int G = mac_group<ORDER>();
+            auto kpair = [&](int q, double(&dst)[TM][TN], auto first) {
                 const int kp = REV ? BK / 2 - 1 - q : q;
                 double2 a2[TM], b2[TN];
 #pragma unroll
@@ -396,30 +399,56 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
                 const double ay[TM] = {a2[0].y, a2[1].y, a2[2].y, a2[3].y};
                 const double bx[TN] = {b2[0].x, b2[1].x, b2[2].x, b2[3].x};
                 const double by[TN] = {b2[0].y, b2[1].y, b2[2].y, b2[3].y};
+                constexpr bool F = decltype(first)::value;
                 if (REV) {
-                    mac16<ACC, RM, mac_group<ORDER>()>(acc, ay, by);
-                    mac16<ACC, RM, mac_group<ORDER>()>(acc, ax, bx);
+                    mac16<ACC, RM, G, F>(dst, ay, by);
+                    mac16<ACC, RM, G>(dst, ax, bx);
                 } else {
-                    mac16<ACC, RM, mac_group<ORDER>()>(acc, ax, bx);
-                    mac16<ACC, RM, mac_group<ORDER>()>(acc, ay, by);
+                    mac16<ACC, RM, G, F>(dst, ax, bx);
+                    mac16<ACC, RM, G>(dst, ay, by);
                 }
-                if constexpr (PAIR && SEG == SEG_TILE) {
-                    if (q == BK / 4 - 1) {  // end of the tile's first leaf of 8
+            };
+            using Fresh = std::integral_constant<bool, true>;
+            using Cont = std::integral_constant<bool, false>;
+            if constexpr (PAIR && SEG == SEG_TILE && ACC <= DRIFT_ACC_FP32) {
+                // The tile is two leaves of 8 (Dot.java:86-102): each starts a
+                // fresh sum, then they combine into the tile's level-1 node.
+                // (FP64/FP32 only: for the narrow accumulators, whose step code
+                // is larger, four copies of it measured 4-18% slower than one
+                // loop that copies and zeroes between the leaves.)
+                double leaf0[TM][TN];
+                kpair(0, leaf0, Fresh{});
+#pragma unroll 1
+                for (int q = 1; q < BK / 4; q++) kpair(q, leaf0, Cont{});
+                kpair(BK / 4, acc, Fresh{});
+#pragma unroll 1
+                for (int q = BK / 4 + 1; q < BK / 2; q++) kpair(q, acc, Cont{});
+                combine<ACC, RM>(leaf0, acc);
+                push(__ffsll(t + 1) - 1, true);    // ctz(t+1) merges in a perfect tree
+            } else {
+                double leaf0[PAIR ? TM : 1][PAIR ? TN : 1];
+                constexpr int kUnroll = kp_unroll<ACC, ORDER>();
+#pragma unroll kUnroll
+                for (int q = 0; q < BK / 2; q++) {
+                    kpair(q, acc, Cont{});
+                    if constexpr (PAIR && SEG == SEG_TILE) {
+                        if (q == BK / 4 - 1) {  // end of the tile's first leaf of 8
 #pragma unroll
-                        for (int i = 0; i < TM; i++)
+                            for (int i = 0; i < TM; i++)
 #pragma unroll
-                            for (int j = 0; j < TN; j++) {
-                                leaf0[i][j] = acc[i][j];
-                                acc[i][j] = 0.0;
-                            }
+                                for (int j = 0; j < TN; j++) {
+                                    leaf0[i][j] = acc[i][j];
+                                    acc[i][j] = 0.0;
+                                }
+                        }
                     }
                 }
-            }
-            if constexpr (SEG == SEG_TILE && PAIR) {
-                combine<ACC, RM>(leaf0, acc);      // the tile's level-1 node
-                push(__ffsll(t + 1) - 1);          // ctz(t+1) merges in a perfect tree
-            } else if constexpr (SEG == SEG_TILE && BLOCK) {
-                if (((t + 1) * BK) % g.acc_block == 0) blocked_fold<ACC>(tot, acc);
+                if constexpr (PAIR && SEG == SEG_TILE) {
+                    combine<ACC, RM>(leaf0, acc);   // the tile's level-1 node
+                    push(__ffsll(t + 1) - 1);       // ctz(t+1) merges in a perfect tree
+                } else if constexpr (SEG == SEG_TILE && BLOCK) {
+                    if (((t + 1) * BK) % g.acc_block == 0) blocked_fold<ACC>(tot, acc);
+                }
             }
         } else {
             // Partial tile, or per-k segment bookkeeping.
