@@ -553,20 +553,22 @@ int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
     const bool fp16 = p->acc == DRIFT_ACC_FP16;
 
     auto scan = [&]() {
-        cudaMemsetAsync(mismatch, 0, sizeof(int), st);
+        if (cudaMemsetAsync(mismatch, 0, sizeof(int), st) != cudaSuccess) return false;
         block_sums_kernel<<<(unsigned)nb, kScanThreads, 0, st>>>(counts, total, chunk, sums);
         scan_sums_kernel<<<1, 32, 0, st>>>(sums, nb);
         apply_offsets_kernel<<<(unsigned)nb, kScanThreads, 0, st>>>(counts, total, chunk, sums,
                                                                     offsets, mismatch);
+        return cudaGetLastError() == cudaSuccess;
     };
     predict_counts_kernel<<<grid, 128, 0, st>>>(g, counts);
-    cudaMemsetAsync(offsets, 0xff, total * sizeof(int64_t), st);  // differs from any offset
-    scan();
+    // Offsets that differ from any real one, so the first scan reports a change.
+    if (cudaMemsetAsync(offsets, 0xff, total * sizeof(int64_t), st) != cudaSuccess || !scan())
+        return DRIFT_ECUDA;
     bool settled = false;
     for (int pass = 0; pass < kMaxSrPasses && !settled; pass++) {
         if (fp16) contract_sr_kernel<DRIFT_ACC_FP16><<<grid, 128, 0, st>>>(g, vals);
         else contract_sr_kernel<DRIFT_ACC_BF16><<<grid, 128, 0, st>>>(g, vals);
-        scan();
+        if (!scan()) return DRIFT_ECUDA;
         int flag = 1;
         if (cudaMemcpyAsync(&flag, mismatch, sizeof(int), cudaMemcpyDeviceToHost, st) !=
                 cudaSuccess ||

@@ -107,4 +107,15 @@ int launch_scale_for(int fmt, const double *amax_now, double *hist, int32_t len,
 int launch_adam(double *p, const double *g, double *m, double *v, int64_t n, double c1, double c2,
                 double lr, int fp32, cudaStream_t st);
 
+// Streaming multiprocessors of the current device (148 on B200), used to size
+// grid-stride launches; 148 if the query fails.
+inline int sm_count() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0)
+        return 148;
+    return sms;
+}
+
 }  // namespace drift

@@ -31,27 +31,24 @@ __global__ void __launch_bounds__(256) fp64_probe_kernel(double seed, int iters,
 }
 
 int launch_fp64_probe(cudaStream_t st, double *ops_per_s) {
-    int sms = 0, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int blocks = sm_count() * 8, iters = 1 << 14;
     double *sink = nullptr;
     if (cudaMallocAsync(&sink, 8, st) != cudaSuccess) return DRIFT_ENOMEM;
-    cudaEvent_t a, b;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
-    const int blocks = sms * 8, iters = 1 << 14;
-    fp64_probe_kernel<<<blocks, 256, 0, st>>>(1.0, 256, sink);  // warm-up
-    cudaEventRecord(a, st);
-    fp64_probe_kernel<<<blocks, 256, 0, st>>>(1.0, iters, sink);
-    cudaEventRecord(b, st);
-    cudaEventSynchronize(b);
+    cudaEvent_t a = nullptr, b = nullptr;
+    bool ok = cudaEventCreate(&a) == cudaSuccess && cudaEventCreate(&b) == cudaSuccess;
     float ms = 0.f;
-    cudaEventElapsedTime(&ms, a, b);
-    cudaEventDestroy(a);
-    cudaEventDestroy(b);
+    if (ok) {
+        fp64_probe_kernel<<<blocks, 256, 0, st>>>(1.0, 256, sink);  // warm-up
+        ok = cudaEventRecord(a, st) == cudaSuccess;
+        fp64_probe_kernel<<<blocks, 256, 0, st>>>(1.0, iters, sink);
+        ok = ok && cudaEventRecord(b, st) == cudaSuccess && cudaEventSynchronize(b) == cudaSuccess &&
+             cudaEventElapsedTime(&ms, a, b) == cudaSuccess && ms > 0.f;
+    }
+    if (a) cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
     cudaFreeAsync(sink, st);
-    cudaStreamSynchronize(st);
-    if (cudaGetLastError() != cudaSuccess) return DRIFT_ECUDA;
+    ok = cudaStreamSynchronize(st) == cudaSuccess && ok;
+    if (!ok || cudaGetLastError() != cudaSuccess) return DRIFT_ECUDA;
     *ops_per_s = (double)blocks * 256 * iters * kProbeChains * 2 / (ms * 1e-3);
     return DRIFT_OK;
 }

@@ -46,9 +46,7 @@ __global__ void __launch_bounds__(256) error_sums_kernel(const double *got, cons
 int launch_error_sums(const double *got, const double *exact, int64_t n, double *sums,
                       cudaStream_t st) {
     if (n <= 0) return DRIFT_OK;
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int sms = sm_count();
     int64_t blocks = (n + 255) / 256;
     if (blocks > sms * 8) blocks = sms * 8;
     error_sums_kernel<<<(unsigned)blocks, 256, 0, st>>>(got, exact, n, sums);
@@ -127,9 +125,7 @@ int launch_radix_pass(const double *got, const double *exact, int64_t n, int pas
     if (cudaMemsetAsync(hist, 0, kRadixBins * sizeof(unsigned long long), st) != cudaSuccess)
         return DRIFT_ECUDA;
     if (n > 0) {
-        int sms = 148, dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const int sms = sm_count();
         int64_t blocks = (n + 255) / 256;
         if (blocks > sms * 4) blocks = sms * 4;
         radix_hist_kernel<<<(unsigned)blocks, 256, 0, st>>>(got, exact, n, pass, state, hist);
