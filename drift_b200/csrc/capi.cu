@@ -666,6 +666,17 @@ int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt, int round
     return rc ? fail(rc, "quantize launch") : DRIFT_OK;
 }
 
+int drift_quantize_draws_dev(drift_ctx *ctx, const drift_policy *p, int fmt, int rounding,
+                             const double *d_src, int64_t n, const double *d_scale, double scale,
+                             int64_t *d_draws, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || n < 0 || !d_draws || (n > 0 && !d_src)) return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_quantize_draws(ctx->ws, p, fmt, rounding, d_src, n, d_scale, scale,
+                               (uint64_t *)d_draws, ctx->d_err(), pick(ctx, stream));
+    return rc ? fail(rc, "draw count launch") : DRIFT_OK;
+}
+
 int drift_per_tensor_scale_dev(drift_ctx *ctx, int fmt, const double *d_amax, double *d_scale,
                                void *stream) {
     int rc = enter(ctx);

@@ -46,6 +46,11 @@ int pairwise_schedule(int64_t K, std::vector<uint8_t> &sched, int *depth);
 
 int launch_amax(const double *d_x, int64_t n, double *d_amax, cudaStream_t st);
 int launch_per_tensor_scale(int fmt, const double *d_amax, double *d_scale, cudaStream_t st);
+// The number of Rng draws a stochastic cast of d_src[0..n) would take
+// (0 for any other rounding), written to *d_draws.
+int launch_quantize_draws(Workspace &ws, const drift_policy *p, int fmt, int rm,
+                          const double *d_src, int64_t n, const double *d_scale, double scale,
+                          uint64_t *d_draws, int *d_err, cudaStream_t st);
 int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const double *d_src,
                     double *d_dst, int64_t n, const double *d_scale, double scale,
                     uint64_t *d_state, unsigned long long *d_clamped, int *d_err,

@@ -379,6 +379,27 @@ int launch_per_tensor_scale(int fmt, const double *d_amax, double *d_scale, cuda
     return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 
+// The cast operator of Quant.quantize for one call (Quant.java:50-123), or
+// an error status.
+static int make_quant_op(const drift_policy *p, int fmt, int rm, const double *d_src,
+                         double *d_dst, const double *d_scale, double scale, QuantOp *op,
+                         int64_t *item_len) {
+    if (!fmt_desc(fmt, &op->f)) return DRIFT_EINVAL;
+    if (rm < 0 || rm > 2) return DRIFT_EINVAL;
+    if (p->scaling < 0 || p->scaling > 2) return DRIFT_EINVAL;
+    if (p->scaling == DRIFT_MX_BLOCK && p->scale_block <= 0) return DRIFT_EINVAL;
+    op->src = d_src;
+    op->dst = d_dst;
+    op->rm = rm;
+    op->scaling = p->scaling;
+    op->headroom = p->mx_headroom;
+    op->d_scale = p->scaling == DRIFT_PER_TENSOR ? d_scale : nullptr;
+    op->scale = scale;
+    op->inv = 1.0 / scale;  // host IEEE division, round to nearest (Quant.java:72)
+    *item_len = p->scaling == DRIFT_MX_BLOCK ? p->scale_block : 32;
+    return DRIFT_OK;
+}
+
 int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const double *d_src,
                     double *d_dst, int64_t n, const double *d_scale, double scale,
                     uint64_t *d_state, unsigned long long *d_clamped, int *d_err,
@@ -392,20 +413,53 @@ int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const
         return DRIFT_OK;
     }
     QuantOp op;
-    if (!fmt_desc(fmt, &op.f)) return DRIFT_EINVAL;
-    if (rm < 0 || rm > 2) return DRIFT_EINVAL;
-    if (p->scaling < 0 || p->scaling > 2) return DRIFT_EINVAL;
-    if (p->scaling == DRIFT_MX_BLOCK && p->scale_block <= 0) return DRIFT_EINVAL;
-    op.src = d_src;
-    op.dst = d_dst;
-    op.rm = rm;
-    op.scaling = p->scaling;
-    op.headroom = p->mx_headroom;
-    op.d_scale = p->scaling == DRIFT_PER_TENSOR ? d_scale : nullptr;
-    op.scale = scale;
-    op.inv = 1.0 / scale;  // host IEEE division, round to nearest (Quant.java:72)
-    const int64_t item_len = p->scaling == DRIFT_MX_BLOCK ? p->scale_block : 32;
+    int64_t item_len = 0;
+    const int rc = make_quant_op(p, fmt, rm, d_src, d_dst, d_scale, scale, &op, &item_len);
+    if (rc) return rc;
     return run_elem(ws, op, n, item_len, rm == DRIFT_STOCHASTIC, d_state, d_clamped, d_err, st);
+}
+
+// Sum of the per-CTA draw counts of a count pass (one CTA).
+__global__ void __launch_bounds__(1024) sum_counts_kernel(const uint64_t *cta_counts,
+                                                          int64_t n_ctas, uint64_t *out) {
+    __shared__ uint64_t s_part[32];
+    uint64_t acc = 0;
+    for (int64_t i = threadIdx.x; i < n_ctas; i += blockDim.x) acc += cta_counts[i];
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) s_part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint64_t t = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += s_part[w];
+        *out = t;
+    }
+}
+
+int launch_quantize_draws(Workspace &ws, const drift_policy *p, int fmt, int rm,
+                          const double *d_src, int64_t n, const double *d_scale, double scale,
+                          uint64_t *d_draws, int *d_err, cudaStream_t st) {
+    if (!d_err || !d_draws) return DRIFT_EINVAL;
+    if (n < 0) return DRIFT_EINVAL;
+    if (fmt == DRIFT_FMT_NONE || rm != DRIFT_STOCHASTIC || n == 0)
+        return cudaMemsetAsync(d_draws, 0, sizeof(uint64_t), st) == cudaSuccess ? DRIFT_OK
+                                                                               : DRIFT_ECUDA;
+    QuantOp op;
+    int64_t item_len = 0;
+    int rc = make_quant_op(p, fmt, rm, d_src, nullptr, d_scale, scale, &op, &item_len);
+    if (rc) return rc;
+    const int64_t items_needed = (n + item_len - 1) / item_len;
+    const int64_t grid = (items_needed + kItemsPerCta - 1) / kItemsPerCta;
+    if (grid > 0x7fffffffLL) return DRIFT_EINVAL;
+    const size_t items = (size_t)grid * kItemsPerCta;
+    char *base = (char *)ws.get(items * sizeof(uint32_t) + (size_t)grid * sizeof(uint64_t) + 256, st);
+    if (!base) return DRIFT_ENOMEM;
+    SrArgs sr{nullptr, nullptr, nullptr, nullptr, nullptr};
+    sr.cta_counts = (uint64_t *)base;
+    sr.item_counts = (uint32_t *)(base + (size_t)grid * sizeof(uint64_t) + 256);
+    sr.err = d_err;  // a NaN into a format without NaN is reported here already
+    elem_kernel<QuantOp, 1><<<(unsigned)grid, kThreads, 0, st>>>(op, n, item_len, sr);
+    sum_counts_kernel<<<1, 1024, 0, st>>>(sr.cta_counts, grid, d_draws);
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 
 int launch_encode(Workspace &ws, int fmt, int rm, const double *d_v, int32_t *d_codes, int64_t n,

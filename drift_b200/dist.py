@@ -1,10 +1,19 @@
-"""Multi-GPU sharding of the policy sweep and the reduction of its statistics.
+"""Multi-GPU sharding of the policy sweep and of single tensors.
 
 The sweep's units are independent (policy, seed) GEMMs, so ranks never
 exchange operands: each rank takes its own seeds and only the statistics are
 combined, with one all-reduce of the error sums and one of the clamp counts
 (NCCL on GPUs, gloo in the CPU tests). Every rank makes the same collective
 calls in the same order.
+
+One tensor can also be cast across ranks, each holding a contiguous shard in
+element order. Its per-tensor scale takes one all-reduce (MAX) of the shards'
+amax. A stochastic cast draws from one Rng stream in element order, so rank
+r starts after the draws of shards 0..r-1: each rank counts its shard's
+draws, one all-gather shares the counts, and each rank casts from the state
+advanced by the earlier shards' total (k draws advance splitmix64's state by
+k * golden). Every rank ends with the state the whole cast leaves, and the
+shards together equal the one-GPU cast bit for bit.
 """
 from __future__ import annotations
 
@@ -81,3 +90,97 @@ def rms_ratio(err_sq: float, exact_sq: float) -> Optional[float]:
     if exact_sq <= 0.0:
         return None
     return math.sqrt(err_sq / exact_sq)
+
+
+# ------------------------------------------------------------------ sharded casts
+
+GOLDEN = 0x9E3779B97F4A7C15
+_MASK64 = (1 << 64) - 1
+
+
+def advance(state: int, draws: int) -> int:
+    """The Rng state after `draws` nextLong calls (Rng.java:17-22)."""
+    return (state + draws * GOLDEN) & _MASK64
+
+
+def shard_bounds(n: int, world: int, rank: int, unit: int = 1):
+    """Element range [lo, hi) of `rank`'s shard of n elements: contiguous, in
+    element order, balanced, with boundaries on multiples of `unit` (the MX
+    block length, so no block is split)."""
+    units = (n + unit - 1) // unit
+    per, extra = divmod(units, world)
+    lo_u = rank * per + min(rank, extra)
+    hi_u = lo_u + per + (1 if rank < extra else 0)
+    return min(n, lo_u * unit), min(n, hi_u * unit)
+
+
+def shard_unit(p) -> int:
+    """Shard boundaries a cast under policy p needs (an MX block never spans two ranks)."""
+    from .kernel import Scaling
+    return p.scale_block if p.scaling == Scaling.MX_BLOCK else 1
+
+
+def count_draws(p, f, rm, src, *, d_scale=None, scale: float = 1.0, stream=None, ctx=None) -> int:
+    """The Rng draws a stochastic cast of this shard takes (0 for other roundings)."""
+    import torch
+    from . import _lib
+    from .kernel import _stream_ptr, _tptr
+
+    ctx = ctx or _lib.Context.current()
+    out = torch.zeros(1, dtype=torch.int64, device=src.device)
+    pc = p.to_c()
+    import ctypes
+    _lib.check(_lib.load().drift_quantize_draws_dev(
+        ctx.handle, ctypes.byref(pc), f.id if f is not None else -1, int(rm), _tptr(src),
+        src.numel(), _tptr(d_scale), float(scale), _tptr(out), _stream_ptr(stream)))
+    return int(out.item())
+
+
+def cast_shard(p, f, rm, src, dst, state: int, draws_before: int, *, d_scale=None,
+               scale: float = 1.0, d_clamped=None, stream=None):
+    """Casts one shard from the stream position after `draws_before` draws."""
+    import torch
+    from .kernel import quantize_dev
+
+    s = advance(state, draws_before)
+    d_state = torch.tensor([s - (1 << 64) if s >> 63 else s], dtype=torch.int64,
+                           device=src.device)
+    quantize_dev(p, f, rm, src, dst, scale=scale, d_scale=d_scale, d_rng_state=d_state,
+                 d_clamped=d_clamped, stream=stream)
+
+
+def sharded_scale(f, src, d_amax, d_scale, dist=None) -> None:
+    """Quant.perTensorScale of the whole tensor from this rank's shard: the
+    local amax, all-reduced with MAX across ranks (amax ignores NaN and is
+    order-free, so this is the one-GPU amax), then the scale, on the device."""
+    from .kernel import amax_dev, per_tensor_scale_dev
+
+    amax_dev(src, d_amax)
+    if dist is not None:
+        dist.all_reduce(d_amax, op=dist.ReduceOp.MAX)
+    per_tensor_scale_dev(f, d_amax, d_scale)
+
+
+def gather_counts(mine: int, dist=None, device=None):
+    """Every rank's draw count, in rank order, and this rank's index: one
+    all-gather of an int64."""
+    import torch
+
+    if dist is None:
+        return [mine], 0
+    t = torch.tensor([mine], dtype=torch.int64, device=device)
+    parts = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t)
+    return [int(x.item()) for x in parts], dist.get_rank()
+
+
+def sharded_quantize(p, f, rm, src, dst, state: int, dist=None, *, d_scale=None,
+                     scale: float = 1.0, d_clamped=None) -> int:
+    """Quant.quantize of a tensor held as one shard per rank (this rank's
+    `src`, element order across ranks by rank). Returns the Rng state after
+    the whole cast, the same on every rank. One all-gather of an int64."""
+    mine = count_draws(p, f, rm, src, d_scale=d_scale, scale=scale)
+    counts, rank = gather_counts(mine, dist, src.device)
+    cast_shard(p, f, rm, src, dst, state, sum(counts[:rank]), d_scale=d_scale, scale=scale,
+               d_clamped=d_clamped)
+    return advance(state, sum(counts))

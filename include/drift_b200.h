@@ -233,6 +233,19 @@ DRIFT_API int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt,
                        uint64_t *d_rng_state, int64_t *d_clamped,
                        void *stream);
 
+/*
+ * The number of Rng draws drift_quantize_dev would take for the same
+ * arguments, written to the device int64 *d_draws, without casting: one read
+ * of d_src. 0 for a rounding other than stochastic. A tensor cast in element
+ * order across ranks (one shard per rank, MX blocks not split) starts rank
+ * r's stream after the draws of shards 0..r-1: the Rng state advanced by k
+ * draws is state + k * 0x9E3779B97F4A7C15 (Rng.java:17-22).
+ */
+DRIFT_API int drift_quantize_draws_dev(drift_ctx *ctx, const drift_policy *p, int fmt,
+                             int rounding, const double *d_src, int64_t n,
+                             const double *d_scale, double scale, int64_t *d_draws,
+                             void *stream);
+
 /* Quant.perTensorScale (java/.../kernel/Quant.java:37-42) from a device amax
  * into a device scale, so a cast can follow an amax without a host trip. */
 DRIFT_API int drift_per_tensor_scale_dev(drift_ctx *ctx, int fmt,
