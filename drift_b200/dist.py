@@ -184,3 +184,103 @@ def sharded_quantize(p, f, rm, src, dst, state: int, dist=None, *, d_scale=None,
     cast_shard(p, f, rm, src, dst, state, sum(counts[:rank]), d_scale=d_scale, scale=scale,
                d_clamped=d_clamped)
     return advance(state, sum(counts))
+
+
+# ------------------------------------------------------------------ sharded GEMM
+
+_GOLDEN_INV = pow(GOLDEN, -1, 1 << 64)  # golden is odd, so k draws are recoverable
+
+# Rounds the last sharded_gemm on this process took (1 when the first guess
+# held; max_rounds + world when it fell back to computing in turn).
+last_gemm_rounds = 0
+
+
+def draws_between(before: int, after: int) -> int:
+    """How many draws took the Rng state from `before` to `after`."""
+    return ((after - before) * _GOLDEN_INV) & _MASK64
+
+
+def _signed(x: int) -> int:
+    return x - (1 << 64) if x >> 63 else x
+
+
+def predicted_draws(p, K: int) -> int:
+    """Draws of one dot when every sum is inexact: one per rounding its order
+    performs (K adds, plus the combines of Dot.pairwise's tree)."""
+    from .kernel import Order
+
+    if K <= 0:
+        return 0
+    if p.order != Order.PAIRWISE:
+        return K
+
+    def leaves(n):
+        return 1 if n <= 8 else leaves(n >> 1) + leaves(n - (n >> 1))
+    return K + leaves(K) - 1
+
+
+def gemm_rows_from(p, A_rows, B, C_rows, state: int, draws_before: int, *, bias=None) -> int:
+    """C_rows = the dots of A_rows against B's rows, the accumulator drawing
+    from the stream position after `draws_before` draws; returns the draws
+    those dots took (0 unless the accumulator is stochastic)."""
+    import torch
+    from .kernel import gemm_dev
+
+    s0 = advance(state, draws_before)
+    d_state = torch.tensor([_signed(s0)], dtype=torch.int64, device=A_rows.device)
+    gemm_dev(p, A_rows, B, C_rows, bias=bias, d_rng_state=d_state)
+    return draws_between(s0, int(d_state.item()) & _MASK64)
+
+
+def stochastic_acc(p) -> bool:
+    from .fmt import Rounding
+    from .kernel import Acc
+
+    return p.acc_rounding == Rounding.STOCHASTIC and p.acc in (Acc.FP16, Acc.BF16)
+
+
+def sharded_gemm(p, A_rows, B, C_rows, state: int, dist=None, *, bias=None,
+                 max_rounds: int = 4) -> int:
+    """A GEMM sharded by row blocks: this rank holds rows [lo, hi) of A (and
+    of C) in rank order, and all of B. Returns the Rng state after the whole
+    GEMM, the same on every rank.
+
+    The dots run in (i, o) order, so a rank's dots draw after every earlier
+    rank's; how many draws those take depends on the draws themselves. The
+    ranks therefore settle the offsets as a fixed point: each computes its
+    rows from a guessed offset and recovers its true count from the state
+    change, one all-gather shares the counts, and the round repeats until the
+    offsets come back unchanged (then every rank used its true offset, by
+    induction from rank 0's, which is always 0). The first guess — every sum
+    inexact — is right unless some sum is exactly representable. After
+    `max_rounds` the ranks compute in turn, each from its predecessors' true
+    counts, which is right for any data."""
+    global last_gemm_rounds
+    if not stochastic_acc(p):
+        from .kernel import gemm_dev
+        gemm_dev(p, A_rows, B, C_rows, bias=bias)
+        last_gemm_rounds = 1
+        return state
+    K, rows, N = A_rows.shape[1], A_rows.shape[0], B.shape[0]
+    mine_guess = rows * N * predicted_draws(p, K)
+    guesses, rank = gather_counts(mine_guess, dist, A_rows.device)
+    offset = sum(guesses[:rank])
+    for rnd in range(max_rounds):
+        true = gemm_rows_from(p, A_rows, B, C_rows, state, offset, bias=bias)
+        counts, _ = gather_counts(true, dist, A_rows.device)
+        prefix = sum(counts[:rank])
+        stable = all(sum(counts[:r]) == sum(guesses[:r]) for r in range(len(counts)))
+        if stable:
+            last_gemm_rounds = rnd + 1
+            return advance(state, sum(counts))
+        guesses, offset = counts, prefix
+    # In turn: rank r computes once ranks 0..r-1 have published their true counts.
+    world = len(guesses)
+    settled = []
+    for r in range(world):
+        mine = gemm_rows_from(p, A_rows, B, C_rows, state, sum(settled), bias=bias) \
+            if r == rank else 0
+        counts, _ = gather_counts(mine, dist, A_rows.device)
+        settled.append(counts[r])
+    last_gemm_rounds = max_rounds + world
+    return advance(state, sum(settled))
