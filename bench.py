@@ -43,6 +43,11 @@ METRIC = "bit-exact emulated MAC/s per policy at 1/2/4/8 B200 vs Java host; mism
 # every operand tile is re-read once per 64-wide output tile.
 DRAM_BYTES_PER_MAC = {"pairwise": 0.159, "other": 0.0566}
 UNIT = "emulated MAC/s"
+# The sweep's policies by name, in order (sweep_policies builds them for the
+# engine; the reference arm, which loads no engine code, names them here).
+SWEEP_NAMES = ["fp32 sequential", "fp32 pairwise", "fp32 blocked", "fp16 sequential",
+               "fp16 pairwise", "fp16 blocked", "bf16 sequential", "bf16 pairwise",
+               "bf16 blocked", "bf16 cast", "e4m3 per-tensor cast", "e4m3 mx32 cast"]
 
 
 def sweep_policies(d):
@@ -428,16 +433,21 @@ def run_reference(args):
     value = statistics.median(vals)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f64", "impl": "reference",
+        "warmup": args.warmup,
+        # A full step's 13 GEMMs at the sampled rate (each timed step is a bounded row sample).
+        "ms_per_step": 13 * float(args.size) ** 3 / value * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "impl": "reference",
         "data": "synthetic: N(0,1) x lognormal(0,1) fp32 values held in doubles",
         "config": {"workload": f"policy sweep GEMM M=N=K={args.size}, 12 policies + exact FP64, "
-                               "row sample", "M": args.size, "N": args.size, "K": args.size},
+                               f"1 seed per rank per step", "M": args.size, "N": args.size,
+                   "K": args.size, "policies": SWEEP_NAMES,
+                   "seeds_per_step": 1, "parallelism": "host threads of rank 0"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "no JVM on this image: the reference's Java path is timed through its C "
-                "restatement (the oracle), with all host threads",
+                "restatement (the oracle), with all host threads, on a bounded row sample of "
+                "each step; ms_per_step is a full step at that rate",
     }
     print(json.dumps(line), flush=True)
     return 0
