@@ -59,3 +59,51 @@ def test_training_step_full_size_first_steps():
         assert (a.view(np.int64) == b.view(np.int64)).all()
     r = got["records"][0]
     assert 0.5 < r.cos <= 1.0 and r.clamp_x >= 0.0
+
+
+# PassTest (java/src/test/java/io/drift/net/PassTest.java:17-24)
+P_VOCAB, P_CTX, P_EMB, P_HIDDEN, P_BATCH = 7, 3, 4, 5, 4
+P_CONTEXTS = np.array([0, 1, 2, 3, 4, 5, 6, 0, 1, 2, 2, 2])
+P_TARGETS = np.array([3, 6, 1, 0])
+
+
+@pytest.mark.gpu
+def test_exact_gradients_match_finite_differences():
+    """PassTest.exactGradientsMatchFiniteDifferences (:26-51): central
+    differences, step 1e-6, worst relative error below 1e-5, the exact
+    policy on the engine. (Weights come from numpy, not java.util.Random.)"""
+    import drift_b200 as d
+    from drift_b200 import mlp
+
+    net = mlp.Net(P_VOCAB, P_CTX, P_EMB, P_HIDDEN, 17)
+    pas = mlp.Pass(d.NumericPolicy.exact(), net, P_BATCH, 1)
+    _, grads = pas.loss_and_grads(P_CONTEXTS, P_TARGETS)
+    h, worst = 1e-6, 0.0
+    for t, params in enumerate(net.tensors()):
+        for i in range(params.size):
+            keep = params[i]
+            params[i] = keep + h
+            up = pas.forward(P_CONTEXTS, P_TARGETS)
+            params[i] = keep - h
+            down = pas.forward(P_CONTEXTS, P_TARGETS)
+            params[i] = keep
+            numeric = (up - down) / (2 * h)
+            err = abs(numeric - grads[t][i]) / max(1e-6, abs(numeric) + abs(grads[t][i]))
+            worst = max(worst, err)
+    assert worst < 1e-5, worst
+
+
+@pytest.mark.gpu
+def test_uncast_fp32_pass_stays_close_to_exact():
+    """PassTest.uncastFp32PassStaysCloseToExact (:69-90): the builder's
+    default policy (FP32 accumulator, no casts) against the exact pass,
+    gradient cosine above 1 - 1e-9."""
+    import drift_b200 as d
+    from drift_b200 import mlp
+
+    net = mlp.Net(P_VOCAB, P_CTX, P_EMB, P_HIDDEN, 17)
+    _, ge = mlp.Pass(d.NumericPolicy.exact(), net, P_BATCH, 1).loss_and_grads(P_CONTEXTS, P_TARGETS)
+    _, gf = mlp.Pass(d.NumericPolicy.builder("fp32").build(), net, P_BATCH, 1).loss_and_grads(
+        P_CONTEXTS, P_TARGETS)
+    a, b = np.concatenate(gf), np.concatenate(ge)
+    assert np.dot(a, b) / np.sqrt(np.dot(b, b) * np.dot(a, a)) > 1 - 1e-9
