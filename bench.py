@@ -565,8 +565,26 @@ def run_train(args):
         attn[pname] = row
     d.check_dev()
 
+    # The stochastically rounded BF16 accumulator (fp8-acc-bf16-sr's contraction):
+    # the training step's forward shape and a square one, device-resident, the
+    # Rng state advancing on the device.
+    sr_pol = d.policies.by_name("fp8-acc-bf16-sr")
+    sr = {}
+    for (Ms, Ns, Ks) in ((64, 2048, 2048), (2048, 2048, 2048)):
+        A = torch.randn(Ms, Ks, dtype=torch.float64, device=dev)
+        Bm = torch.randn(Ns, Ks, dtype=torch.float64, device=dev)
+        C = torch.empty(Ms, Ns, dtype=torch.float64, device=dev)
+        st = torch.tensor([1], dtype=torch.int64, device=dev)
+        d.gemm_dev(sr_pol, A, Bm, C, d_rng_state=st)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            d.gemm_dev(sr_pol, A, Bm, C, d_rng_state=st)
+        torch.cuda.synchronize()
+        sr[f"{Ms}x{Ns}x{Ks}"] = Ms * Ns * Ks * args.steps / (time.perf_counter() - t0)
+
     print(json.dumps({"mode": "train", "policy": p.name, "macs_per_step": macs,
-                      "attention_mac_per_s": attn,
+                      "attention_mac_per_s": attn, "sr_accumulator_mac_per_s": sr,
                       "config": {"vocab": 96, "ctx": 32, "emb": 64, "hidden": 2048, "batch": 64},
                       "device_resident": {"s_per_step": dev_s, "mac_per_s": macs / dev_s,
                                           "steps": args.steps},

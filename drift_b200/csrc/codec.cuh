@@ -11,19 +11,40 @@
 
 namespace drift {
 
+// Integer parts of a non-negative x < 2^52 on the FP64 pipe: with 2^52 added,
+// the unit in the last place is 1, so the add itself rounds x to an integer
+// (to nearest even, or toward zero), and subtracting 2^52 again is exact.
+__device__ __forceinline__ double rint_small(double x) {
+    return __dsub_rn(__dadd_rn(x, 0x1p52), 0x1p52);
+}
+__device__ __forceinline__ double floor_small(double x) {
+    return __dsub_rn(__dadd_rz(x, 0x1p52), 0x1p52);
+}
+
+// A draw's 53 random bits as a double, exactly: the low 52 bits under the
+// exponent of 2^52, less 2^52, plus the top bit's 2^52 (no integer
+// conversion instruction).
+__device__ __forceinline__ double u53_to_double(uint64_t u) {
+    const double lo = __dsub_rn(
+        __longlong_as_double((long long)(0x4330000000000000ULL | (u & 0xFFFFFFFFFFFFFULL))),
+        0x1p52);
+    return (u >> 52) ? __dadd_rn(lo, 0x1p52) : lo;
+}
+
 // Rounds the exact, non-negative `scaled` to an integer under `rm`
 // (MiniFloat.roundToIntegral, MiniFloat.java:258-278). For STOCHASTIC, `drew`
 // reports whether the fraction was non-zero, i.e. whether Java would have
 // consumed a draw; u53 holds that draw's 53 random bits.
 __device__ __forceinline__ double round_integral(double scaled, int rm, uint64_t u53,
                                                  bool &drew) {
-    if (rm == DRIFT_NEAREST_EVEN) return rint(scaled);
-    double fl = floor(scaled);
+    // `scaled` is below 2^(mant+1) <= 2^11 for every format.
+    if (rm == DRIFT_NEAREST_EVEN) return rint_small(scaled);
+    double fl = floor_small(scaled);
     if (rm == DRIFT_TRUNCATE) return fl;
     double frac = __dsub_rn(scaled, fl);  // exact
     if (frac == 0.0) return fl;
     drew = true;
-    return __dmul_rn((double)u53, 0x1p-53) < frac ? fl + 1.0 : fl;
+    return __dmul_rn(u53_to_double(u53), 0x1p-53) < frac ? fl + 1.0 : fl;
 }
 
 // MiniFloat.encode(v, rm, rng) (MiniFloat.java:156-211). Sets `drew` when a

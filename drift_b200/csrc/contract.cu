@@ -83,13 +83,13 @@ __device__ __forceinline__ double sr_round(double x, uint64_t state, uint64_t id
     if (e < F::min_exp) e = F::min_exp;
     const int q = e - F::mant;
     const double scaled = __dmul_rn(ax, pow2(-q));  // exact
-    const double fl = floor(scaled);
+    const double fl = floor_small(scaled);  // scaled < 2^(mant+1)
     const double frac = __dsub_rn(scaled, fl);
     double m = fl;
     if (frac != 0.0) {
         const uint64_t u = draw_u53(state, idx + cnt);
         cnt++;
-        if (__dmul_rn((double)u, 0x1p-53) < frac) m = fl + 1.0;
+        if (__dmul_rn(u53_to_double(u), 0x1p-53) < frac) m = fl + 1.0;
     }
     double r = __dmul_rn(m, pow2(q));
     if (r > F::max()) r = F::max();
