@@ -73,8 +73,10 @@ __device__ __forceinline__ void window_of(const ContractArgs &g, int64_t i, int6
 
 // Dot.round(x, acc, STOCHASTIC, rng) (Dot.java:141-182), drawing the
 // (idx + cnt)-th number of the stream only when the fraction is non-zero.
+// `z` is the splitmix64 counter of the next draw, state + (idx + cnt + 1) *
+// golden; a dot's draws are consecutive, so it advances by golden per draw.
 template <int ACC>
-__device__ __forceinline__ double sr_round(double x, uint64_t state, uint64_t idx, uint32_t &cnt) {
+__device__ __forceinline__ double sr_round(double x, uint64_t &z, uint32_t &cnt) {
     using F = AccFmt<ACC>;
     if (x == 0.0 || isnan(x)) return x;
     const double ax = fabs(x);
@@ -87,7 +89,8 @@ __device__ __forceinline__ double sr_round(double x, uint64_t state, uint64_t id
     const double frac = __dsub_rn(scaled, fl);
     double m = fl;
     if (frac != 0.0) {
-        const uint64_t u = draw_u53(state, idx + cnt);
+        const uint64_t u = splitmix_mix(z) >> 11;  // draw_u53(state, idx + cnt)
+        z += kGolden;
         cnt++;
         if (__dmul_rn(u53_to_double(u), 0x1p-53) < frac) m = fl + 1.0;
     }
@@ -109,9 +112,10 @@ template <int ACC, int RM> struct ExactRounder {
 };
 
 template <int ACC> struct SrRounder {
-    uint64_t state, idx;
+    uint64_t z;  // counter of the next draw: state + (first index + cnt + 1) * golden
     uint32_t cnt;
-    __device__ double operator()(double t) { return sr_round<ACC>(t, state, idx, cnt); }
+    __device__ SrRounder(uint64_t state, uint64_t idx) : z(state + (idx + 1) * kGolden), cnt(0) {}
+    __device__ double operator()(double t) { return sr_round<ACC>(t, z, cnt); }
 };
 
 // Dot.dot (Dot.java:26-121) over n terms a[k*a_k] * b[k*b_k], any order.
@@ -265,7 +269,7 @@ __device__ __forceinline__ double sr_output(const ContractArgs &g, int64_t out, 
     if (g.causal && o > i) return 0.0;
     int64_t lo, n;
     window_of(g, i, lo, n);
-    SrRounder<ACC> rnd{*g.state, idx, 0};
+    SrRounder<ACC> rnd(*g.state, idx);
     double v = dot_any<ACC>(g, g.A + t * g.a_batch + i * g.a_row + lo * g.a_k,
                             g.B + t * g.b_batch + o * g.b_col + lo * g.b_k, n, rnd);
     cnt = rnd.cnt;
