@@ -593,6 +593,50 @@ def run_train(args):
     return 0
 
 
+def run_configs(args):
+    """The other study configurations, timed end to end on one GPU (inputs
+    generated first, results read back): the dot sweep (200 seeds x lengths
+    16..4096, 10 policies + exact), the real-shape batch (4096 x 64 x 2048,
+    7 policies + exact) and the block-scaled GEMM (4096^3, 6 policies +
+    exact). Wall-clock seconds, emulated MACs and MAC/s, with each study's
+    headline figures."""
+    import torch
+    from drift_b200 import sweeps
+
+    out = {}
+    lengths = tuple(2 ** k for k in range(4, 13))
+    sweeps.dot_sweep_dev(lengths=(16,), seeds=2)   # warm-up
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ds = sweeps.dot_sweep_dev(lengths=lengths, seeds=200)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    macs = 11 * 200 * sum(lengths)
+    t = ds["table"]
+    out["dot_sweep"] = {"seconds": dt, "macs": macs, "mac_per_s": macs / dt,
+                        "median_rel_error_at_4096": {k: v[4096]["median_rel_error"]
+                                                      for k, v in t.items()}}
+    X, W = sweeps.real_dot_inputs()
+    sweeps.real_dot_batch(X[:64], W)   # warm-up
+    t0 = time.perf_counter()
+    rd = sweeps.real_dot_batch(X, W)
+    dt = time.perf_counter() - t0
+    macs = 8 * X.shape[0] * W.shape[0] * X.shape[1]
+    out["real_dot_batch"] = {"seconds": dt, "macs": macs, "mac_per_s": macs / dt,
+                             "path": "host-buffer entry points", "stats": rd}
+    sweeps.mx_gemm(512)   # warm-up
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    mx = sweeps.mx_gemm(4096)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    macs = 7 * 4096 ** 3
+    out["mx_gemm"] = {"seconds": dt, "macs": macs, "mac_per_s": macs / dt,
+                      "path": "device-resident", "stats": mx}
+    print(json.dumps({"mode": "configs", **out}), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -604,7 +648,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
-    ap.add_argument("--mode", choices=["sweep", "kernels", "train"], default="sweep",
+    ap.add_argument("--mode", choices=["sweep", "kernels", "train", "configs"], default="sweep",
                     help="kernels: time each policy's contraction alone (for profiling)")
     ap.add_argument("--policies", default="", help="kernels mode: comma-separated policy names")
     args = ap.parse_args()
@@ -616,6 +660,8 @@ def main() -> int:
         return run_kernels(args)
     if args.mode == "train":
         return run_train(args)
+    if args.mode == "configs":
+        return run_configs(args)
     return run_engine(args)
 
 

@@ -102,6 +102,64 @@ def dot_sweep(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)), seed
     return {"table": table, "rows": rows}
 
 
+def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
+                  seeds: int = 200, policies: Optional[List[NumericPolicy]] = None,
+                  sigma: float = 1.0, device: int = 0) -> Dict:
+    """dot_sweep with every dot of one (policy, length) in one batched
+    contraction on the device: the seeds' vectors are the rows of two
+    seeds x n tensors and the dots a batch of 1 x 1 contractions. The casts
+    follow DotSweep.run (DotSweep.java:112-122) per seed: the vector's own
+    per-tensor scale, a then b on the seed's Rng(0xD1F7 + seed). Same inputs,
+    outputs and rows as dot_sweep."""
+    import torch
+
+    from .kernel import (amax_dev, check_dev, contract_dev, contraction, per_tensor_scale_dev,
+                         quantize_dev)
+
+    policies = policies or dot_sweep_policies()
+    dev = torch.device("cuda", device)
+    exact_p = NumericPolicy.exact()
+    table: Dict[str, Dict[int, Dict[str, float]]] = {p.name: {} for p in policies}
+    rows = []
+    scal = torch.zeros(2, dtype=torch.float64, device=dev)
+    for n in lengths:
+        ab = []
+        for seed in range(seeds):
+            rs = np.random.default_rng(seed * 7919 + n)
+            ab.append((heavy_tailed(rs, n, sigma), heavy_tailed(rs, n, sigma)))
+        A = torch.from_numpy(np.stack([a for a, _ in ab])).to(dev)
+        B = torch.from_numpy(np.stack([b for _, b in ab])).to(dev)
+        op = contraction(batch=seeds, rows=1, cols=1, depth=n, a_batch=n, a_row=0, a_k=1,
+                         b_batch=n, b_col=0, b_k=1, c_batch=1, c_row=1)
+        exact = torch.empty(seeds, dtype=torch.float64, device=dev)
+        contract_dev(exact_p, op, A, B, exact)
+        ex = exact.cpu().numpy()
+        for p in policies:
+            f = p.input_format
+            qa, qb = A, B
+            cl = torch.zeros(seeds, dtype=torch.int64, device=dev)
+            if f is not None:
+                qa, qb = torch.empty_like(A), torch.empty_like(B)
+                for seed in range(seeds):
+                    st = torch.tensor([0xD1F7 + seed], dtype=torch.int64, device=dev)
+                    for src, dst in ((A[seed], qa[seed]), (B[seed], qb[seed])):
+                        amax_dev(src, scal[0:1])
+                        per_tensor_scale_dev(f, scal[0:1], scal[1:2])
+                        quantize_dev(p, f, p.input_rounding, src, dst, d_scale=scal[1:2],
+                                     d_rng_state=st, d_clamped=cl[seed:seed + 1])
+            got = torch.empty(seeds, dtype=torch.float64, device=dev)
+            contract_dev(p, op, qa, qb, got)
+            check_dev()
+            v, c = got.cpu().numpy(), cl.cpu().numpy()
+            errs = np.abs(v - ex) / np.abs(ex)
+            for seed in range(seeds):
+                rows.append((p.name, n, seed, float(v[seed]), float(ex[seed]), int(c[seed])))
+            e = np.sort(errs)
+            table[p.name][n] = {"median_rel_error": float(e[len(e) // 2]),
+                                "clamped_per_pair": float(c.sum()) / seeds}
+    return {"table": table, "rows": rows}
+
+
 def real_dot_policies() -> List[NumericPolicy]:
     """The real-shape batch's 7 policies: FP32/FP16/BF16 sequential, FP16/BF16
     pairwise, the e4m3 per-tensor cast and the bf16 cast (from
@@ -201,7 +259,9 @@ def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0) -> 
     counts them) and per pair of 32-blocks."""
     import torch
 
-    from .kernel import amax_dev, check_dev, gemm_dev, per_tensor_scale_dev, quantize_dev
+    from .kernel import (amax_dev, check_dev, error_sums_dev, gemm_dev, per_tensor_scale_dev,
+                         quantize_dev)
+    from .stats import upper_median_rel_error
 
     dev = torch.device("cuda", device)
     g = torch.Generator(device=dev)
@@ -228,12 +288,14 @@ def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0) -> 
                 quantize_dev(p, f, Rounding.NEAREST_EVEN, src, dst, d_clamped=cl[k:k + 1])
         gemm_dev(p, qa, qw, C)
         check_dev()
-        rel = ((C - exact).abs() / exact.abs()).flatten()
-        err_sq = float(((C - exact) ** 2).sum())
-        ex_sq = float((exact ** 2).sum())
+        # Statistics on the engine's own kernels: the upper median by radix
+        # selection, the RMS ratio from two device sums.
+        sums = torch.zeros(2, dtype=torch.float64, device=dev)
+        error_sums_dev(C, exact, sums)
+        err_sq, ex_sq = (float(x) for x in sums.cpu())
         ca, cw = (int(x) for x in cl.cpu())
         per_pair = ca / size + cw / size
-        res[p.name] = {"median_rel_error": float(rel.kthvalue(rel.numel() // 2 + 1).values),
+        res[p.name] = {"median_rel_error": upper_median_rel_error(C, exact, C.numel()),
                        "rms_error_ratio": float(np.sqrt(err_sq / ex_sq)),
                        "clamped_per_pair": per_pair,
                        "clamped_per_block_pair": per_pair / (size // 32)}

@@ -112,3 +112,21 @@ def test_mx_gemm_sampled_outputs():
         assert (got.view(np.int64) == want.view(np.int64)).all(), p.name
     res = sweeps.mx_gemm(1024, policies=sweeps.mx_policies()[:2])
     assert res["e4m3 mx32 spec"]["clamped_per_pair"] > 0.0
+
+
+def test_device_dot_sweep_equals_host_sweep():
+    """dot_sweep_dev (one batched contraction per policy and length) gives
+    the same rows as dot_sweep (one host call per dot): values, exact values,
+    clamp counts and the summary table."""
+    from drift_b200 import sweeps
+
+    host = sweeps.dot_sweep(lengths=(16, 100, 1024), seeds=7)
+    dev = sweeps.dot_sweep_dev(lengths=(16, 100, 1024), seeds=7)
+    key = lambda r: (r[0], r[1], r[2])
+    h, g = sorted(host["rows"], key=key), sorted(dev["rows"], key=key)
+    assert len(h) == len(g)
+    for a, b in zip(h, g):
+        assert a[:3] == b[:3] and a[5] == b[5]
+        assert np.float64(a[3]).view(np.int64) == np.float64(b[3]).view(np.int64), a[:3]
+        assert np.float64(a[4]).view(np.int64) == np.float64(b[4]).view(np.int64), a[:3]
+    assert host["table"] == dev["table"]
