@@ -84,6 +84,8 @@ SIGNATURES = {
                                   _vp, _vp, _vp]),
     "drift_quantize_dev_noalloc": (_int, [_P(DriftPolicy), _int, _int, _vp, _vp, _i64, _vp, _d,
                                           _vp, _vp, _vp, _vp]),
+    "drift_quantize_rows_dev": (_int, [_vp, _P(DriftPolicy), _int, _int, _vp, _vp, _i64, _i64,
+                                       _vp, _vp]),
     "drift_quantize_draws_dev": (_int, [_vp, _P(DriftPolicy), _int, _int, _vp, _i64, _vp, _d,
                                         _vp, _vp]),
     "drift_per_tensor_scale_dev": (_int, [_vp, _int, _vp, _vp, _vp]),

@@ -666,6 +666,19 @@ int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt, int round
     return rc ? fail(rc, "quantize launch") : DRIFT_OK;
 }
 
+int drift_quantize_rows_dev(drift_ctx *ctx, const drift_policy *p, int fmt, int rounding,
+                            const double *d_src, double *d_dst, int64_t rows, int64_t len,
+                            int64_t *d_clamped, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!p || rows < 0 || len < 0 || (rows * len > 0 && (!d_src || !d_dst)))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_quantize_rows(p, fmt, rounding, d_src, d_dst, rows, len,
+                              (unsigned long long *)d_clamped, ctx->d_err(), pick(ctx, stream));
+    return rc ? fail(rc, "row-wise cast (stochastic rounding and MX scaling are per tensor)")
+              : DRIFT_OK;
+}
+
 int drift_quantize_draws_dev(drift_ctx *ctx, const drift_policy *p, int fmt, int rounding,
                              const double *d_src, int64_t n, const double *d_scale, double scale,
                              int64_t *d_draws, void *stream) {

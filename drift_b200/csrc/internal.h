@@ -51,6 +51,11 @@ int launch_per_tensor_scale(int fmt, const double *d_amax, double *d_scale, cuda
 int launch_quantize_draws(Workspace &ws, const drift_policy *p, int fmt, int rm,
                           const double *d_src, int64_t n, const double *d_scale, double scale,
                           uint64_t *d_draws, int *d_err, cudaStream_t st);
+// `rows` tensors of `len` elements cast one by one, each with its own
+// per-tensor scale; clamps added per row. Nearest-even or truncate, no MX.
+int launch_quantize_rows(const drift_policy *p, int fmt, int rm, const double *d_src,
+                         double *d_dst, int64_t rows, int64_t len,
+                         unsigned long long *d_clamped, int *d_err, cudaStream_t st);
 int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const double *d_src,
                     double *d_dst, int64_t n, const double *d_scale, double scale,
                     uint64_t *d_state, unsigned long long *d_clamped, int *d_err,

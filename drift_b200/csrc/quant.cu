@@ -419,6 +419,71 @@ int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const
     return run_elem(ws, op, n, item_len, rm == DRIFT_STOCHASTIC, d_state, d_clamped, d_err, st);
 }
 
+// ------------------------------------------------------------------ row-wise casts
+//
+// `rows` tensors of `len` elements each (row r at src + r*len), every one cast
+// as Quant.quantize casts one tensor, with its own per-tensor scale
+// (Quant.perTensorScale of its own amax): DotSweep.run casts each vector so
+// (DotSweep.java:112-122). One CTA per row: the row's amax, its scale, then
+// QuantOp's element cast, clamps counted per row.
+constexpr int kRowThreads = 256;
+
+__global__ void __launch_bounds__(kRowThreads) rows_cast_kernel(QuantOp op, int64_t len,
+                                                                unsigned long long *clamped,
+                                                                int *d_err) {
+    __shared__ double s_max[kRowThreads / 32];
+    __shared__ unsigned s_cl[kRowThreads / 32];
+    const int64_t base = (int64_t)blockIdx.x * len;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (op.scaling == DRIFT_PER_TENSOR) {
+        double m = 0.0;  // Quant.amax: NaN never wins
+        for (int64_t i = threadIdx.x; i < len; i += blockDim.x) m = fmax(m, fabs(op.src[base + i]));
+        m = warp_max(m);
+        if (lane == 0) s_max[warp] = m;
+        __syncthreads();
+        m = 0.0;
+        for (int w = 0; w < kRowThreads / 32; w++) m = fmax(m, s_max[w]);
+        op.scale = (m == 0.0 || !isfinite(m)) ? 1.0 : __ddiv_rn(op.f.max_finite, m);
+        op.inv = __ddiv_rn(1.0, op.scale);  // Quant.java:37-42, :72
+    }
+    const QuantOp::Item it{1.0, 1.0, false};
+    int err = 0;
+    unsigned clamps = 0;
+    for (int64_t i = threadIdx.x; i < len; i += blockDim.x) {
+        bool clamp = false;
+        op.apply(it, base + i, op.src[base + i], 0, clamp, err);
+        clamps += clamp;
+    }
+    for (int o = 16; o > 0; o >>= 1) clamps += __shfl_xor_sync(0xffffffffu, clamps, o);
+    if (lane == 0) s_cl[warp] = clamps;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long t = 0;
+        for (int w = 0; w < kRowThreads / 32; w++) t += s_cl[w];
+        if (clamped) clamped[blockIdx.x] += t;
+    }
+    if (err) atomicOr(d_err, err);
+}
+
+int launch_quantize_rows(const drift_policy *p, int fmt, int rm, const double *d_src,
+                         double *d_dst, int64_t rows, int64_t len,
+                         unsigned long long *d_clamped, int *d_err, cudaStream_t st) {
+    if (rows < 0 || len < 0 || rows > 0x7fffffffLL) return DRIFT_EINVAL;
+    if (rm == DRIFT_STOCHASTIC || p->scaling == DRIFT_MX_BLOCK) return DRIFT_EINVAL;
+    if (rows == 0 || len == 0) return DRIFT_OK;
+    if (fmt == DRIFT_FMT_NONE)  // Quant.java:58-61: a plain copy
+        return d_dst == d_src || cudaMemcpyAsync(d_dst, d_src, rows * len * sizeof(double),
+                                                 cudaMemcpyDeviceToDevice, st) == cudaSuccess
+                   ? DRIFT_OK
+                   : DRIFT_ECUDA;
+    QuantOp op;
+    int64_t item_len = 0;
+    const int rc = make_quant_op(p, fmt, rm, d_src, d_dst, nullptr, 1.0, &op, &item_len);
+    if (rc) return rc;
+    rows_cast_kernel<<<(unsigned)rows, kRowThreads, 0, st>>>(op, len, d_clamped, d_err);
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+}
+
 // Sum of the per-CTA draw counts of a count pass (one CTA).
 __global__ void __launch_bounds__(1024) sum_counts_kernel(const uint64_t *cta_counts,
                                                           int64_t n_ctas, uint64_t *out) {

@@ -370,6 +370,19 @@ def quantize_dev(p: NumericPolicy, f: Optional[MiniFloat], rm: Rounding, src, ds
         _tptr(d_clamped), _stream_ptr(stream)))
 
 
+def quantize_rows_dev(p: NumericPolicy, f: Optional[MiniFloat], rm: Rounding, src, dst, *,
+                      d_clamped=None, stream=None, ctx=None) -> None:
+    """Each row of the 2-D tensor src cast as its own tensor (its own
+    per-tensor scale under PER_TENSOR scaling), one launch; clamps added to
+    d_clamped[row]. Nearest-even or truncate, no MX scaling."""
+    ctx = ctx or _lib.Context.current()
+    pc = p.to_c()
+    rows, length = src.shape
+    _lib.check(_lib.load().drift_quantize_rows_dev(
+        ctx.handle, ctypes.byref(pc), f.id if f is not None else -1, int(rm), _tptr(src),
+        _tptr(dst), rows, length, _tptr(d_clamped), _stream_ptr(stream)))
+
+
 def amax_dev(x, d_amax, *, stream=None, ctx=None) -> None:
     ctx = ctx or _lib.Context.current()
     _lib.check(_lib.load().drift_amax_dev(ctx.handle, _tptr(x), x.numel(), _tptr(d_amax),

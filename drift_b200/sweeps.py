@@ -114,7 +114,7 @@ def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
     import torch
 
     from .kernel import (amax_dev, check_dev, contract_dev, contraction, per_tensor_scale_dev,
-                         quantize_dev)
+                         quantize_dev, quantize_rows_dev)
 
     policies = policies or dot_sweep_policies()
     dev = torch.device("cuda", device)
@@ -138,7 +138,13 @@ def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
             f = p.input_format
             qa, qb = A, B
             cl = torch.zeros(seeds, dtype=torch.int64, device=dev)
-            if f is not None:
+            rowwise = (f is not None and p.input_rounding != Rounding.STOCHASTIC
+                       and p.scaling != Scaling.MX_BLOCK)
+            if rowwise:  # every vector its own tensor, one launch per operand
+                qa, qb = torch.empty_like(A), torch.empty_like(B)
+                quantize_rows_dev(p, f, p.input_rounding, A, qa, d_clamped=cl)
+                quantize_rows_dev(p, f, p.input_rounding, B, qb, d_clamped=cl)
+            elif f is not None:
                 qa, qb = torch.empty_like(A), torch.empty_like(B)
                 for seed in range(seeds):
                     st = torch.tensor([0xD1F7 + seed], dtype=torch.int64, device=dev)

@@ -234,6 +234,19 @@ DRIFT_API int drift_quantize_dev(drift_ctx *ctx, const drift_policy *p, int fmt,
                        void *stream);
 
 /*
+ * `rows` tensors of `len` doubles each (row r at d_src + r*len), each cast as
+ * drift_quantize_dev casts one tensor, with its own per-tensor scale
+ * (Quant.perTensorScale of the row's own amax) under PER_TENSOR scaling:
+ * DotSweep.run's cast of every vector (java/.../tools/DotSweep.java:112-122),
+ * one launch for all of them. Clamps are added to d_clamped[r] (int64, may
+ * be NULL). Nearest-even or truncate only, and no MX scaling: DRIFT_EINVAL
+ * otherwise (cast such rows one by one).
+ */
+DRIFT_API int drift_quantize_rows_dev(drift_ctx *ctx, const drift_policy *p, int fmt,
+                            int rounding, const double *d_src, double *d_dst,
+                            int64_t rows, int64_t len, int64_t *d_clamped, void *stream);
+
+/*
  * The number of Rng draws drift_quantize_dev would take for the same
  * arguments, written to the device int64 *d_draws, without casting: one read
  * of d_src. 0 for a rounding other than stochastic. A tensor cast in element

@@ -131,3 +131,40 @@ def test_nan_into_finite_format_raises(d):
     with pytest.raises(d.DriftError) as e:
         d.Quant.quantize(np.array([1.0, np.nan]), 0, np.zeros(2), 0, 2, d.Formats.E2M1, p, 1.0, None)
     assert e.value.status == 2
+
+
+@pytest.mark.parametrize("name", ["fp8", "fp8-e4m3-grads", "bf16", "mxfp4"])
+def test_rowwise_casts_equal_one_cast_per_row(d, name):
+    """drift_quantize_rows_dev against drift_quantize on each row: values and
+    clamps (rows with zeros, infinities and a NaN included). MX and stochastic
+    rounding are refused: they are cast one tensor at a time."""
+    import torch
+
+    p = d.policies.by_name(name)
+    f = p.input_format
+    rs = np.random.default_rng(3)
+    rows, n = 9, 777
+    X = heavy_tailed(rs, rows * n).reshape(rows, n)
+    X[2] = 0.0
+    X[3, 5] = np.inf
+    X[4, 7] = np.nan if f.specials != d.Specials.FINITE else 1.0
+    src = torch.from_numpy(X).cuda()
+    dst = torch.empty_like(src)
+    cl = torch.zeros(rows, dtype=torch.int64, device="cuda")
+    if p.scaling == d.Scaling.MX_BLOCK:
+        with pytest.raises(d.DriftError):
+            d.kernel.quantize_rows_dev(p, f, p.input_rounding, src, dst, d_clamped=cl)
+        return
+    d.kernel.quantize_rows_dev(p, f, p.input_rounding, src, dst, d_clamped=cl)
+    d.check_dev()
+    got, gcl = dst.cpu().numpy(), cl.cpu().numpy()
+    for r in range(rows):
+        s = d.Quant.per_tensor_scale(f, d.Quant.amax(X[r])) if p.scaling == d.Scaling.PER_TENSOR \
+            else 1.0
+        want = np.empty(n)
+        c = d.Quant.quantize(X[r], 0, want, 0, n, f, p, s, None)
+        assert_bits(got[r], want, f"{name} row {r}")
+        assert gcl[r] == c
+    sr = p.to_builder("sr").input_rounding(d.Rounding.STOCHASTIC).build()
+    with pytest.raises(d.DriftError):
+        d.kernel.quantize_rows_dev(sr, f, d.Rounding.STOCHASTIC, src, dst)
