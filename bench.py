@@ -308,6 +308,15 @@ def run_engine(args):
     traffic_per_launch = M * N * K * (n_pair * DRAM_BYTES_PER_MAC["pairwise"] +
                                       (len(pols) + 1 - n_pair) * DRAM_BYTES_PER_MAC["other"]) \
         / (len(pols) + 1)
+    # The HBM view of the same launches: their DRAM traffic over their time,
+    # against the measured copy bandwidth of this pool's B200s.
+    hbm_peak, hbm_src = 6650.0, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
+    try:
+        hbm_peak = float(json.load(open(REPO / "MEASURED_PEAKS.json"))["hbm_gbs"])
+        hbm_src = "MEASURED_PEAKS.json hbm_gbs"
+    except (OSError, KeyError, ValueError):
+        pass
+    hbm_gbs = traffic_per_launch * (len(pols) + 1) / (gemm_total_ms * 1e-3) / 1e9
     per_policy = {"exact fp64": M * N * K / (gemm_ms[0] * 1e-3)}
     for k, p in enumerate(pols):
         per_policy[p.name] = M * N * K / (gemm_ms[k + 1] * 1e-3)
@@ -351,6 +360,10 @@ def run_engine(args):
                      "traffic": traffic_per_launch,
                      "traffic_unit": "bytes per contraction launch, averaged over the step's 13",
                      "kernel": "gemm_kernel (all policies)",
+                     "hbm_view": {"achieved": hbm_gbs, "peak": hbm_peak, "unit": "GB/s",
+                                  "frac": hbm_gbs / hbm_peak, "peak_source": hbm_src,
+                                  "note": "DRAM traffic of the contraction launches (per-MAC "
+                                          "bytes from the ncu capture) over their time"},
                      "peak_source": "measured DMUL+DADD probe (drift_probe_fp64) on this GPU"},
         "per_policy_mac_per_s": per_policy,
         "stats": stats,
