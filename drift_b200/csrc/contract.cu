@@ -119,10 +119,10 @@ template <int ACC> struct SrRounder {
 };
 
 // Dot.dot (Dot.java:26-121) over n terms a[k*a_k] * b[k*b_k], any order.
-template <int ACC, class R>
-__device__ double dot_any(const ContractArgs &g, const double *a, const double *b, int64_t n,
-                          R &rnd) {
-    auto term = [&](int64_t k) { return __dmul_rn(__ldg(a + k * g.a_k), __ldg(b + k * g.b_k)); };
+// `term(k)` is the k-th product of the window (k from 0); it is called with
+// the k of Dot.dot's evaluation order, so a caller may stage the operands.
+template <int ACC, class T, class R>
+__device__ double dot_terms(const ContractArgs &g, T term, int64_t n, R &rnd) {
     // The adds form one dependent chain; the products do not. With a rounding
     // accumulator the chain is long, so eight products are formed ahead of
     // their adds and their loads are in flight together. An FP64 chain is a
@@ -194,6 +194,14 @@ __device__ double dot_any(const ContractArgs &g, const double *a, const double *
         }
     }
     return vals[0];
+}
+
+template <int ACC, class R>
+__device__ double dot_any(const ContractArgs &g, const double *a, const double *b, int64_t n,
+                          R &rnd) {
+    return dot_terms<ACC>(
+        g, [&](int64_t k) { return __dmul_rn(__ldg(a + k * g.a_k), __ldg(b + k * g.b_k)); }, n,
+        rnd);
 }
 
 // Leaves of Dot.pairwise's tree over n terms. Node sizes on one level differ
@@ -289,6 +297,56 @@ __global__ void __launch_bounds__(128) contract_sr_kernel(const ContractArgs g, 
         vals[out] = sr_output<ACC>(g, out, (uint64_t)g.offsets[out], cnt);
         g.counts[out] = cnt;
     }
+}
+
+// ------------------------------------------------------------ staged stochastic pass
+//
+// With a FULL window every dot has the same length and order, so every thread
+// of a CTA asks for the same terms in the same sequence (for pairwise, the
+// same tree). A CTA of 16 x 16 outputs of one problem stages its operands in
+// shared memory KC terms at a time: when a thread needs a k outside the staged
+// chunk, every thread does, and they refill it together between two
+// barriers. The products then come from shared memory instead of a pair of
+// global loads per term. Threads past the matrix edge take part in every
+// refill and store nothing, so the CTA's control flow stays uniform.
+constexpr int kStageSide = 16;
+constexpr int kStageK = 32;
+
+template <int ACC>
+__global__ void __launch_bounds__(kStageSide *kStageSide)
+    contract_sr_staged_kernel(const ContractArgs g, double *vals) {
+    __shared__ double sA[kStageSide][kStageK + 1], sB[kStageSide][kStageK + 1];
+    const int tx = threadIdx.x % kStageSide, ty = threadIdx.x / kStageSide;
+    const int64_t t = blockIdx.z;
+    const int64_t i0 = (int64_t)blockIdx.y * kStageSide, o0 = (int64_t)blockIdx.x * kStageSide;
+    const int64_t i = i0 + ty, o = o0 + tx;
+    const bool live = i < g.rows && o < g.cols;
+    const double *At = g.A + t * g.a_batch, *Bt = g.B + t * g.b_batch;
+    int64_t k0 = -kStageK;  // start of the staged chunk (none yet)
+    auto stage = [&](int64_t base) {
+        __syncthreads();  // every thread has finished with the previous chunk
+        for (int e = threadIdx.x; e < kStageSide * kStageK; e += kStageSide * kStageSide) {
+            const int r = e / kStageK, c = e % kStageK;  // consecutive threads walk k
+            const int64_t k = base + c;
+            const bool kin = k < g.depth;
+            sA[r][c] = (kin && i0 + r < g.rows) ? __ldg(At + (i0 + r) * g.a_row + k * g.a_k) : 0.0;
+            sB[r][c] = (kin && o0 + r < g.cols) ? __ldg(Bt + (o0 + r) * g.b_col + k * g.b_k) : 0.0;
+        }
+        __syncthreads();
+        k0 = base;
+    };
+    auto term = [&](int64_t k) {
+        if (k < k0 || k >= k0 + kStageK) stage(k - k % kStageK);  // the same k in every thread
+        return __dmul_rn(sA[ty][k - k0], sB[tx][k - k0]);
+    };
+    const int64_t out = (t * g.rows + i) * g.cols + o;
+    SrRounder<ACC> rnd(*g.state, live ? (uint64_t)g.offsets[out] : 0);
+    double v = dot_terms<ACC>(g, term, g.depth, rnd);
+    if (!live) return;
+    if (g.alpha != 1.0) v = __dmul_rn(v, g.alpha);
+    if (g.bias) v = __dadd_rn(v, g.bias[o]);
+    vals[out] = v;
+    g.counts[out] = rnd.cnt;
 }
 
 // The dots in order, one thread: the fallback that is correct for any data.
@@ -555,6 +613,12 @@ int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
     g.offsets = offsets;
     g.counts = counts;
     const bool fp16 = p->acc == DRIFT_ACC_FP16;
+    // FULL windows without a mask take the staged pass (every dot the same shape).
+    const int64_t sx = (d.op.cols + kStageSide - 1) / kStageSide;
+    const int64_t sy = (d.op.rows + kStageSide - 1) / kStageSide;
+    const bool staged = d.op.window == DRIFT_WINDOW_FULL && !d.op.causal && d.op.depth > 0 &&
+                        sx <= 0x7fffffffLL && sy <= 65535 && d.op.batch <= 65535;
+    const dim3 sgrid((unsigned)sx, (unsigned)sy, (unsigned)d.op.batch);
 
     auto scan = [&]() {
         if (cudaMemsetAsync(mismatch, 0, sizeof(int), st) != cudaSuccess) return false;
@@ -570,8 +634,13 @@ int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
         return DRIFT_ECUDA;
     bool settled = false;
     for (int pass = 0; pass < kMaxSrPasses && !settled; pass++) {
-        if (fp16) contract_sr_kernel<DRIFT_ACC_FP16><<<grid, 128, 0, st>>>(g, vals);
-        else contract_sr_kernel<DRIFT_ACC_BF16><<<grid, 128, 0, st>>>(g, vals);
+        if (staged) {
+            if (fp16) contract_sr_staged_kernel<DRIFT_ACC_FP16><<<sgrid, kStageSide * kStageSide, 0, st>>>(g, vals);
+            else contract_sr_staged_kernel<DRIFT_ACC_BF16><<<sgrid, kStageSide * kStageSide, 0, st>>>(g, vals);
+        } else {
+            if (fp16) contract_sr_kernel<DRIFT_ACC_FP16><<<grid, 128, 0, st>>>(g, vals);
+            else contract_sr_kernel<DRIFT_ACC_BF16><<<grid, 128, 0, st>>>(g, vals);
+        }
         if (!scan()) return DRIFT_ECUDA;
         int flag = 1;
         if (cudaMemcpyAsync(&flag, mismatch, sizeof(int), cudaMemcpyDeviceToHost, st) !=
