@@ -33,7 +33,7 @@ def _rank_main(rank, world, port, out):
 
 def test_two_gloo_ranks_reduce_statistics():
     world = 2
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:  # no fork after CUDA use
         out = m.dict()
         mp.spawn(_rank_main, args=(world, _free_port(), out), nprocs=world, join=True)
         res = dict(out)

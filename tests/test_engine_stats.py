@@ -65,7 +65,7 @@ def test_union_median_over_two_ranks():
     import torch.multiprocessing as mp
 
     world = 2
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:  # no fork after CUDA use
         out = m.dict()
         mp.spawn(_rank, args=(world, _free_port(), out), nprocs=world, join=True)
         res = dict(out)
