@@ -91,6 +91,7 @@ SIGNATURES = {
     "drift_per_tensor_scale_dev": (_int, [_vp, _int, _vp, _vp, _vp]),
     "drift_gemm_dev": (_int, [_vp, _P(DriftPolicy), _i64, _i64, _i64, _vp, _i64, _i64, _vp,
                               _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
+    "drift_gemm_route": (_int, [_vp, _P(_int), _vp]),
     "drift_error_sums_dev": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "drift_radix_hist_dev": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp]),
     "drift_radix_select_dev": (_int, [_vp, _int, _vp, _vp, _vp]),

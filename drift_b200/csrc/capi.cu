@@ -146,12 +146,13 @@ struct drift_ctx {
     Workspace io;       // staging for host-buffer calls
     ScheduleCache sched;
     // Small device words: [0] error flags (int), [8] rng state, [16] clamp
-    // counter, [24] scalar result.
+    // counter, [24] scalar result, [32] the last GEMM's route (int).
     char *d_small = nullptr;
     int *d_err() { return (int *)d_small; }
     uint64_t *d_state() { return (uint64_t *)(d_small + 8); }
     unsigned long long *d_clamped() { return (unsigned long long *)(d_small + 16); }
     double *d_scalar() { return (double *)(d_small + 24); }
+    int *d_route() { return (int *)(d_small + 32); }
 };
 
 static int enter(drift_ctx *ctx) {
@@ -602,7 +603,8 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
                 break;
             }
             rc = launch_gemm(ctx->ws, ctx->sched, p, rows, N, K, d_a + off, a_row_stride, 1, d_b,
-                             b_row_stride, b_k_stride, d_bias, d_c + r0 * N, N, ctx->d_err(), st);
+                             b_row_stride, b_k_stride, d_bias, d_c + r0 * N, N, ctx->d_err(),
+                             ctx->d_route(), st);
             if (rc) {
                 rc = fail(rc, "gemm launch");
                 break;
@@ -629,7 +631,7 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
                              ctx->d_state(), ctx->d_err(), st);
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
-                         b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), st);
+                         b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), ctx->d_route(), st);
     }
     if (rc) return fail(rc, "gemm launch");
     CUDA_TRY(cudaMemcpy2DAsync(C, c_row_stride * 8, d_c, N * 8, N * 8, M, cudaMemcpyDeviceToHost, st),
@@ -726,9 +728,22 @@ int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, 
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
                          b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->d_err(),
-                         pick(ctx, stream));
+                         ctx->d_route(), pick(ctx, stream));
     }
     return rc ? fail(rc, "gemm launch") : DRIFT_OK;
+}
+
+int drift_gemm_route(drift_ctx *ctx, int *route, void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!route) return fail(DRIFT_EINVAL, "null route");
+    cudaStream_t st = pick(ctx, stream);
+    int r = 0;
+    CUDA_TRY(cudaMemcpyAsync(&r, ctx->d_route(), sizeof(int), cudaMemcpyDeviceToHost, st),
+             "read route");
+    CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+    *route = r;
+    return DRIFT_OK;
 }
 
 // Lowest and highest element index an affine access off + sum(coef_j * x_j),

@@ -54,6 +54,7 @@
 
 #include "codec.cuh"
 #include "internal.h"
+#include "tma.cuh"
 
 namespace drift {
 
@@ -64,7 +65,6 @@ constexpr int STAGE_DOUBLES = (BM + BN) * LDK;   // one A tile and one B tile
 constexpr int TILE_BYTES = BM * LDK * (int)sizeof(double);  // 9 KiB per operand per stage
 // Stages plus the stage barriers.
 constexpr int GEMM_SMEM = STAGES * STAGE_DOUBLES * (int)sizeof(double) + 64;
-constexpr long long kWaitLimit = 1LL << 22;  // try_wait rounds before giving up
 constexpr int kMaxPairwiseDepth = 30;  // stack depth; enough for any int32 K
 // Unroll of the k-pair loop of a full tile, chosen by measurement on B200:
 // the narrow accumulators' rounding makes a long tile body fall out of the
@@ -95,6 +95,9 @@ struct GemmArgs {
     // and for a TMA operand the same stride in rows of its map.
     int64_t a_bs, b_bs, c_bs;
     int64_t a_brows, b_brows;
+    // When set, the kernel leaves at once if the word reads nonzero: the FP32
+    // path (gemm32.cu) took the call.
+    const int *skip;
 };
 
 // Offset, in doubles, of element (row, k) of a staged operand tile.
@@ -203,45 +206,10 @@ __device__ __forceinline__ void combine(const double (&left)[TM][TN], double (&r
     round16<ACC, RM>(right);
 }
 
-__device__ __forceinline__ unsigned smem_addr(const void *p) {
-    return (unsigned)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-// Bounded wait for the barrier's phase `parity` to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
-    const unsigned a = smem_addr(bar);
-    for (long long i = 0; i < kWaitLimit; i++) {
-        unsigned done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-            " selp.u32 %0, 1, 0, p;\n}"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
-}
-
 // One 18 x 64 box of doubles (k0 .. k0+17 of rows r0 .. r0+63) into a tile.
 __device__ __forceinline__ void tma_load_box(double *dst, const CUtensorMap *map, int k0, int r0,
                                              uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(k0), "r"(r0), "r"(smem_addr(bar))
-        : "memory");
+    tma_load_2d(dst, map, k0, r0, bar);
 }
 
 // The register loader: rows [r0, r0+64) x k [k0, k0+16) of any-strided X into
@@ -271,6 +239,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
     constexpr bool PAIR = ORDER == DRIFT_PAIRWISE;
     constexpr bool BLOCK = ORDER == DRIFT_BLOCKED;
 
+    if (g.skip && *g.skip) return;
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
     const int64_t m0 = (int64_t)blockIdx.y * BM;
@@ -563,27 +532,6 @@ static int launch_order(int order, int seg, const GemmArgs &g, const CUtensorMap
     }
 }
 
-// cuTensorMapEncodeTiled, found through the runtime (no libcuda link).
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_tiled() {
-    static EncodeTiledFn fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
 // A TMA map of a K-contiguous operand: dims {K, rows}, row stride rs doubles,
 // 18 x 64 boxes (a padded tile), zero fill outside. TMA needs a 16-byte
 // aligned base and a row stride that is a multiple of 16 bytes; every box
@@ -605,12 +553,29 @@ static bool make_map(CUtensorMap *map, const double *X, int64_t rows, int64_t rs
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+static int gemm_batched(ScheduleCache &cache, const drift_policy *p, int64_t batch, int64_t M,
+                        int64_t N, int64_t K, const double *A, int64_t a_rs, int64_t a_ks,
+                        int64_t a_bs, const double *B, int64_t b_rs, int64_t b_ks, int64_t b_bs,
+                        const double *bias, double *C, int64_t c_rs, int64_t c_bs, int *d_err,
+                        const int *skip, cudaStream_t st);
+
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
-                int *d_err, cudaStream_t st) {
-    return launch_gemm_batched(ws, cache, p, 1, M, N, K, A, a_rs, a_ks, 0, B, b_rs, b_ks, 0, bias,
-                               C, c_rs, 0, d_err, st);
+                int *d_err, int *d_route, cudaStream_t st) {
+    if (M < 0 || N < 0 || K < 0 || a_rs < 0 || a_ks < 0 || b_rs < 0 || b_ks < 0 || c_rs < 0 ||
+        p->acc < 0 || p->acc > 3 || p->order < 0 || p->order > 3)
+        return DRIFT_EINVAL;
+    // FP32 accumulation over narrow products may go to the FP32 pipe; the
+    // decision is made on the device, and this launch stands down if taken.
+    const int *skip = nullptr;
+    int rc = launch_gemm_f32(ws, p, M, N, K, A, a_rs, a_ks, B, b_rs, b_ks, bias, C, c_rs, d_err,
+                             d_route, st, &skip);
+    if (rc) return rc;
+    if (!skip && d_route && cudaMemsetAsync(d_route, 0, sizeof(int), st) != cudaSuccess)
+        return DRIFT_ECUDA;
+    return gemm_batched(cache, p, 1, M, N, K, A, a_rs, a_ks, 0, B, b_rs, b_ks, 0, bias, C, c_rs, 0,
+                        d_err, skip, st);
 }
 
 int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t batch,
@@ -619,6 +584,15 @@ int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy 
                         int64_t b_bs, const double *bias, double *C, int64_t c_rs, int64_t c_bs,
                         int *d_err, cudaStream_t st) {
     (void)ws;
+    return gemm_batched(cache, p, batch, M, N, K, A, a_rs, a_ks, a_bs, B, b_rs, b_ks, b_bs, bias, C,
+                        c_rs, c_bs, d_err, nullptr, st);
+}
+
+static int gemm_batched(ScheduleCache &cache, const drift_policy *p, int64_t batch, int64_t M,
+                        int64_t N, int64_t K, const double *A, int64_t a_rs, int64_t a_ks,
+                        int64_t a_bs, const double *B, int64_t b_rs, int64_t b_ks, int64_t b_bs,
+                        const double *bias, double *C, int64_t c_rs, int64_t c_bs, int *d_err,
+                        const int *skip, cudaStream_t st) {
     if (M < 0 || N < 0 || K < 0 || a_rs < 0 || a_ks < 0 || b_rs < 0 || b_ks < 0 || c_rs < 0)
         return DRIFT_EINVAL;
     if (batch < 0 || a_bs < 0 || b_bs < 0 || c_bs < 0 || batch > 65535) return DRIFT_EINVAL;
@@ -646,6 +620,7 @@ int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy 
     g.c_rs = c_rs;
     g.acc_block = std::max<int64_t>(1, p->acc_block);  // Dot.java:105
     g.err = d_err;
+    g.skip = skip;
     CUtensorMap ma, mb;
     memset(&ma, 0, sizeof(ma));
     memset(&mb, 0, sizeof(mb));

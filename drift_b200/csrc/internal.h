@@ -95,10 +95,22 @@ int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy 
                         int64_t b_bs, const double *bias, double *C, int64_t c_rs, int64_t c_bs,
                         int *d_err, cudaStream_t st);
 int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
+// One contraction C = A B^T (+ bias). `d_route`, when given, receives 1 if
+// the call ran on the FP32 pipe (gemm32.cu) and 0 otherwise.
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
-                int *d_err, cudaStream_t st);
+                int *d_err, int *d_route, cudaStream_t st);
+// gemm32.cu: queues the FP32-pipe path of an FP32-accumulated contraction
+// whose policy and shape qualify (an operand scan, a device-side decision and
+// the FFMA contraction, which stands down unless the scan allows it). Sets
+// *skip to the decision word the double-precision contraction must then
+// check, or leaves it null when the path does not apply to this call. Uses
+// `ws` for the scan and the transposed operands.
+int launch_gemm_f32(Workspace &ws, const drift_policy *p, int64_t M, int64_t N, int64_t K,
+                    const double *A, int64_t a_rs, int64_t a_ks, const double *B, int64_t b_rs,
+                    int64_t b_ks, const double *bias, double *C, int64_t c_rs, int *d_err,
+                    int *d_route, cudaStream_t st, const int **skip);
 
 // tables.cu
 int launch_value_table(int fmt, uint64_t *d_bits, cudaStream_t st);

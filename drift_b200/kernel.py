@@ -403,6 +403,16 @@ def error_sums_dev(got, exact, d_sums, *, stream=None, ctx=None) -> None:
                                                 got.numel(), _tptr(d_sums), _stream_ptr(stream)))
 
 
+def gemm_route(stream=None, ctx=None) -> int:
+    """The path of the context's last non-stochastic GEMM: 1 for the FP32 pipe
+    (narrow products under an FP32 accumulator), 0 for the double-precision
+    contraction. Synchronises the stream."""
+    ctx = ctx or _lib.Context.current()
+    out = ctypes.c_int()
+    _lib.check(_lib.load().drift_gemm_route(ctx.handle, ctypes.byref(out), _stream_ptr(stream)))
+    return out.value
+
+
 def probe_fp64(ctx=None) -> float:
     """The FP64 pipe's measured DMUL+DADD rate, in operations per second."""
     ctx = ctx or _lib.Context.current()

@@ -309,6 +309,15 @@ DRIFT_API int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
                    const double *d_bias, double *d_C, int64_t c_row_stride,
                    uint64_t *d_rng_state, void *stream);
 
+/* Which path the context's most recent drift_gemm / drift_gemm_dev with a
+ * non-stochastic accumulator took: *route = 1 if it ran on the FP32 pipe
+ * (an FP32 accumulator, sequential, reversed or blocked in chunks of a
+ * multiple of 16, at least 2^27 multiply-accumulates, and every product of
+ * the two operands an exact fp32 number, so that Dot.java's (float)(s + a*b)
+ * is one fp32 FMA), 0 if it ran on the double-precision contraction. Both
+ * give the same bits; the route is a performance fact. Waits for `stream`. */
+DRIFT_API int drift_gemm_route(drift_ctx *ctx, int *route, void *stream);
+
 /* Error sums of RealDotSweep's RMS ratio
  * (java/.../tools/RealDotSweep.java:245-257): ADDS sum((got-exact)^2) to
  * d_sums[0] and sum(exact^2) to d_sums[1]. */
