@@ -233,6 +233,14 @@ def run_engine(args):
           for _ in range(n_pol + 1)]
     gemm_ms = [0.0] * (n_pol + 1)
     launches = [0]
+    # Each contraction's route (drift_gemm_route), read in the first warm-up
+    # step: route 0 is one launch; routes 1 (FP32 pipe) and 2 (scanned, stayed
+    # on the double-precision kernel) are five (two operand scans, the
+    # decision, and both contractions, one of which stands down at once).
+    routes = [None] * (n_pol + 1)
+
+    def gemm_launches(k):
+        return 1 if not routes[k] else 5
 
     def cast(p, src, dst, slot, counter):
         f = p.input_format
@@ -249,17 +257,22 @@ def run_engine(args):
             launches[0] += 1
         return dst
 
-    def step(timed_gemms: bool):
+    def step(read_routes: bool):
         ev[0][0].record(stream)
         d.gemm_dev(exact_p, A, B, Cx, ctx=ctx)
         ev[0][1].record(stream)
-        launches[0] += 1
+        if read_routes:
+            routes[0] = d.gemm_route(ctx=ctx)
+        launches[0] += gemm_launches(0)
         for k, p in enumerate(pols):
             a = cast(p, A, qA, 0, clamps[k, 0:1])
             b = cast(p, B, qB, 1, clamps[k, 1:2])
             ev[k + 1][0].record(stream)
             d.gemm_dev(p, a, b, C, ctx=ctx)
             ev[k + 1][1].record(stream)
+            if read_routes:
+                routes[k + 1] = d.gemm_route(ctx=ctx)
+            launches[0] += gemm_launches(k + 1) - 1
             d.error_sums_dev(C, Cx, sums[k], ctx=ctx)
             # DotSweep's summary statistic over every rank's outputs: the upper
             # median of the relative errors (DotSweep.java:152-153).
@@ -274,8 +287,8 @@ def run_engine(args):
             pg.barrier()
             torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step(False)
+    for w in range(args.warmup):
+        step(w == 0)
     d.check_dev(ctx=ctx)
     barrier()
     sums.zero_()
@@ -298,16 +311,25 @@ def run_engine(args):
     macs_per_step_rank = (n_pol + 1) * M * N * K
     value = macs_per_step_rank * world * args.steps / (ms_max * 1e-3)
 
-    # Roofline of the dominant kernel (the contraction): FP64-pipe work is 2
-    # operations (DMUL + DADD) per emulated MAC; the peak is this GPU's
-    # measured DMUL+DADD rate.
+    # Roofline of the dominant kernel, the double-precision contraction
+    # (gemm_kernel, every contraction not on the FP32 pipe): FP64-pipe work is
+    # 2 operations (DMUL + DADD) per emulated MAC; the peak is this GPU's
+    # measured DMUL+DADD rate. The FP32-pipe contractions (gemm_f32_kernel)
+    # get their own line: one FFMA per MAC against the measured FFMA rate.
     fp64_peak = d.probe_fp64(ctx)
-    gemm_total_ms = sum(gemm_ms)
-    achieved = 2.0 * macs_per_step_rank / (gemm_total_ms * 1e-3)
-    n_pair = sum(1 for p in pols if p.order == d.Order.PAIRWISE)
+    fp32_peak = d.probe_fp32(ctx)
+    on_fp32 = [k for k in range(n_pol + 1) if routes[k] == d.ROUTE_FP32]
+    on_fp64 = [k for k in range(n_pol + 1) if routes[k] != d.ROUTE_FP32]
+    gemm_total_ms = sum(gemm_ms[k] for k in on_fp64)
+    achieved = 2.0 * len(on_fp64) * M * N * K / (gemm_total_ms * 1e-3)
+    fp32_ms = sum(gemm_ms[k] for k in on_fp32)
+    fp32_achieved = len(on_fp32) * M * N * K / (fp32_ms * 1e-3) if on_fp32 else 0.0
+    all_pols = [exact_p] + list(pols)
+    names = ["exact fp64"] + [p.name for p in pols]
+    n_pair = sum(1 for k in on_fp64 if all_pols[k].order == d.Order.PAIRWISE)
     traffic_per_launch = M * N * K * (n_pair * DRAM_BYTES_PER_MAC["pairwise"] +
-                                      (len(pols) + 1 - n_pair) * DRAM_BYTES_PER_MAC["other"]) \
-        / (len(pols) + 1)
+                                      (len(on_fp64) - n_pair) * DRAM_BYTES_PER_MAC["other"]) \
+        / len(on_fp64)
     # The HBM view of the same launches: their DRAM traffic over their time,
     # against the measured copy bandwidth of this pool's B200s.
     hbm_peak, hbm_src = 6650.0, "fallback 6.65 TB/s (no MEASURED_PEAKS.json)"
@@ -316,7 +338,7 @@ def run_engine(args):
         hbm_src = "MEASURED_PEAKS.json hbm_gbs"
     except (OSError, KeyError, ValueError):
         pass
-    hbm_gbs = traffic_per_launch * (len(pols) + 1) / (gemm_total_ms * 1e-3) / 1e9
+    hbm_gbs = traffic_per_launch * len(on_fp64) / (gemm_total_ms * 1e-3) / 1e9
     per_policy = {"exact fp64": M * N * K / (gemm_ms[0] * 1e-3)}
     for k, p in enumerate(pols):
         per_policy[p.name] = M * N * K / (gemm_ms[k + 1] * 1e-3)
@@ -358,13 +380,23 @@ def run_engine(args):
         "roofline": {"bound": "fp64", "achieved": achieved / 1e12, "peak": fp64_peak / 1e12,
                      "unit": "TFLOP/s", "frac": achieved / fp64_peak,
                      "traffic": traffic_per_launch,
-                     "traffic_unit": "bytes per contraction launch, averaged over the step's 13",
-                     "kernel": "gemm_kernel (all policies)",
+                     "traffic_unit": "bytes per double-precision contraction launch, averaged "
+                                     "over the step's launches of it",
+                     "kernel": "gemm_kernel",
+                     "contractions": [names[k] for k in on_fp64],
                      "hbm_view": {"achieved": hbm_gbs, "peak": hbm_peak, "unit": "GB/s",
                                   "frac": hbm_gbs / hbm_peak, "peak_source": hbm_src,
                                   "note": "DRAM traffic of the contraction launches (per-MAC "
                                           "bytes from the ncu capture) over their time"},
-                     "peak_source": "measured DMUL+DADD probe (drift_probe_fp64) on this GPU"},
+                     "peak_source": "measured DMUL+DADD probe (drift_probe_fp64) on this GPU",
+                     "fp32_pipe": {"kernel": "gemm_f32_kernel",
+                                   "contractions": [names[k] for k in on_fp32],
+                                   "achieved": fp32_achieved / 1e12, "peak": fp32_peak / 1e12,
+                                   "unit": "TFMA/s", "frac": fp32_achieved / fp32_peak,
+                                   "peak_source": "measured FFMA probe (drift_probe_fp32) on "
+                                                  "this GPU",
+                                   "note": "one FFMA per emulated MAC; the time includes the "
+                                           "operand scans and the decision"}},
         "per_policy_mac_per_s": per_policy,
         "stats": stats,
         "e2e": e2e,
@@ -482,24 +514,40 @@ def run_kernels(args):
     B = (torch.randn(S, S, device=dev, generator=g) *
          torch.exp(torch.randn(S, S, device=dev, generator=g))).double()
     C = torch.empty_like(A)
+    qA, qB = torch.empty_like(A), torch.empty_like(B)
+    scal = torch.zeros((4,), dtype=torch.float64, device=dev)
     pols = [d.NumericPolicy.exact()] + sweep_policies(d)
     if args.policies:
         keep = [x.strip() for x in args.policies.split(",")]
         pols = [p for p in pols if p.name in keep]
     stream = torch.cuda.current_stream()
-    out = {}
+    out, routes = {}, {}
     for p in pols:
-        d.gemm_dev(p, A, B, C)
+        # The policy's input cast, as in the sweep step, outside the timing.
+        a, b = A, B
+        if p.input_format is not None:
+            a, b = qA, qB
+            for k, (src, dst) in enumerate(((A, qA), (B, qB))):
+                if p.scaling == d.Scaling.PER_TENSOR:
+                    d.amax_dev(src, scal[k:k + 1])
+                    d.per_tensor_scale_dev(p.input_format, scal[k:k + 1], scal[2 + k:3 + k])
+                    d.quantize_dev(p, p.input_format, p.input_rounding, src, dst,
+                                   d_scale=scal[2 + k:3 + k])
+                else:
+                    d.quantize_dev(p, p.input_format, p.input_rounding, src, dst)
+        d.gemm_dev(p, a, b, C)
+        routes[p.name] = d.gemm_route()
         if args.steps > 0:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
             for _ in range(args.steps):
-                d.gemm_dev(p, A, B, C)
+                d.gemm_dev(p, a, b, C)
             e1.record(stream)
             torch.cuda.synchronize()
             out[p.name] = args.steps * S ** 3 / (e0.elapsed_time(e1) * 1e-3)
     d.check_dev()
-    print(json.dumps({"mode": "kernels", "size": S, "mac_per_s": out}), flush=True)
+    print(json.dumps({"mode": "kernels", "size": S, "mac_per_s": out, "routes": routes}),
+          flush=True)
     return 0
 
 

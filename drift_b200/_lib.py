@@ -102,6 +102,7 @@ SIGNATURES = {
     "drift_scale_for_dev": (_int, [_vp, _int, _vp, _vp, _i32, _vp, _vp, _vp]),
     "drift_adam_dev": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i32, _d, _i32, _vp]),
     "drift_probe_fp64": (_int, [_vp, _P(_d)]),
+    "drift_probe_fp32": (_int, [_vp, _P(_d)]),
     "drift_check_dev": (_int, [_vp, _vp]),
 }
 

@@ -870,6 +870,14 @@ int drift_probe_fp64(drift_ctx *ctx, double *ops_per_s) {
     return rc ? fail(rc, "fp64 probe") : DRIFT_OK;
 }
 
+int drift_probe_fp32(drift_ctx *ctx, double *fma_per_s) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!fma_per_s) return fail(DRIFT_EINVAL, "null out");
+    rc = launch_fp32_probe(ctx->stream, fma_per_s);
+    return rc ? fail(rc, "fp32 probe") : DRIFT_OK;
+}
+
 int drift_quantize_dev_noalloc(const drift_policy *p, int fmt, int rounding, const double *d_src,
                                double *d_dst, int64_t n, const double *d_scale, double scale,
                                uint64_t *d_rng_state, int64_t *d_clamped, int *d_err,

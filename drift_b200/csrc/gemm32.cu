@@ -150,7 +150,7 @@ __global__ void f32_decide_kernel(int *props, int *route) {
     // 2^(ta+tb+2), and a product of at most 24 bits below 2^128 is finite.
     if (!za && !zb) ok = ok && wa + wb <= 24 && la + lb >= -149 && ta + tb + 2 <= 128;
     props[kFlagWord] = ok ? 1 : 0;
-    if (route) *route = ok ? 1 : 0;
+    if (route) *route = ok ? DRIFT_ROUTE_FP32 : DRIFT_ROUTE_SCANNED;
 }
 
 struct F32Args {

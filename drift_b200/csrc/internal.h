@@ -95,6 +95,7 @@ int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy 
                         int64_t b_bs, const double *bias, double *C, int64_t c_rs, int64_t c_bs,
                         int *d_err, cudaStream_t st);
 int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
+int launch_fp32_probe(cudaStream_t st, double *fma_per_s);
 // One contraction C = A B^T (+ bias). `d_route`, when given, receives 1 if
 // the call ran on the FP32 pipe (gemm32.cu) and 0 otherwise.
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,

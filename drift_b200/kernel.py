@@ -403,10 +403,15 @@ def error_sums_dev(got, exact, d_sums, *, stream=None, ctx=None) -> None:
                                                 got.numel(), _tptr(d_sums), _stream_ptr(stream)))
 
 
+ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED = 0, 1, 2
+
+
 def gemm_route(stream=None, ctx=None) -> int:
-    """The path of the context's last non-stochastic GEMM: 1 for the FP32 pipe
-    (narrow products under an FP32 accumulator), 0 for the double-precision
-    contraction. Synchronises the stream."""
+    """The path of the context's last non-stochastic GEMM: ROUTE_FP32 for the
+    FP32 pipe (narrow products under an FP32 accumulator), ROUTE_SCANNED for a
+    candidate whose operands kept it on the double-precision contraction,
+    ROUTE_DOUBLE for the double-precision contraction alone. Synchronises the
+    stream."""
     ctx = ctx or _lib.Context.current()
     out = ctypes.c_int()
     _lib.check(_lib.load().drift_gemm_route(ctx.handle, ctypes.byref(out), _stream_ptr(stream)))
@@ -418,6 +423,14 @@ def probe_fp64(ctx=None) -> float:
     ctx = ctx or _lib.Context.current()
     out = ctypes.c_double()
     _lib.check(_lib.load().drift_probe_fp64(ctx.handle, ctypes.byref(out)))
+    return out.value
+
+
+def probe_fp32(ctx=None) -> float:
+    """The FP32 pipe's measured FFMA rate, in fused multiply-adds per second."""
+    ctx = ctx or _lib.Context.current()
+    out = ctypes.c_double()
+    _lib.check(_lib.load().drift_probe_fp32(ctx.handle, ctypes.byref(out)))
     return out.value
 
 

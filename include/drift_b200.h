@@ -310,12 +310,22 @@ DRIFT_API int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
                    uint64_t *d_rng_state, void *stream);
 
 /* Which path the context's most recent drift_gemm / drift_gemm_dev with a
- * non-stochastic accumulator took: *route = 1 if it ran on the FP32 pipe
- * (an FP32 accumulator, sequential, reversed or blocked in chunks of a
- * multiple of 16, at least 2^27 multiply-accumulates, and every product of
- * the two operands an exact fp32 number, so that Dot.java's (float)(s + a*b)
- * is one fp32 FMA), 0 if it ran on the double-precision contraction. Both
- * give the same bits; the route is a performance fact. Waits for `stream`. */
+ * non-stochastic accumulator took (for a host-buffer call that travelled in
+ * row chunks, its last chunk):
+ *   DRIFT_ROUTE_DOUBLE   0  the double-precision contraction (one launch);
+ *   DRIFT_ROUTE_FP32     1  the FP32 pipe: an FP32 accumulator, sequential,
+ *                          reversed or blocked in chunks of a multiple of 16,
+ *                          at least 2^27 multiply-accumulates, and every
+ *                          product of the two operands an exact fp32 number,
+ *                          so that Dot.java's (float)(s + a*b) is one fp32 FMA;
+ *   DRIFT_ROUTE_SCANNED  2  a candidate for the FP32 pipe whose operand scan
+ *                          kept it on the double-precision contraction.
+ * Every route gives the same bits; the route is a performance fact (routes 1
+ * and 2 launch five kernels: two scans, the decision and both contractions,
+ * one of which stands down). Waits for `stream`. */
+#define DRIFT_ROUTE_DOUBLE 0
+#define DRIFT_ROUTE_FP32 1
+#define DRIFT_ROUTE_SCANNED 2
 DRIFT_API int drift_gemm_route(drift_ctx *ctx, int *route, void *stream);
 
 /* Error sums of RealDotSweep's RMS ratio
@@ -435,6 +445,11 @@ DRIFT_API int drift_adam_dev(drift_ctx *ctx, double *d_param, const double *d_gr
  * rate on the context's device (operations per second), the denominator of
  * the contraction's roofline. Takes a few milliseconds. */
 DRIFT_API int drift_probe_fp64(drift_ctx *ctx, double *ops_per_s);
+
+/* No counterpart in the reference: measures the FP32 pipe's FFMA issue rate
+ * (fused multiply-adds per second), the denominator of the FP32-pipe
+ * contraction's roofline (drift_gemm_route). Takes a few milliseconds. */
+DRIFT_API int drift_probe_fp32(drift_ctx *ctx, double *fma_per_s);
 
 /*
  * Synchronises `stream` and returns the first device-side error raised since

@@ -5,10 +5,11 @@ runs as one fp32 FMA per multiply-accumulate; it must still give the bits of
 Dot.java's (float)(s + a*b) chain (Dot.java:50-56), its reversed walk
 (:72-84) and BLOCKED's fold (:104-121). Each case also reads which path ran
 (drift_gemm_route): narrow operands (bf16 casts, MX-scaled minifloats, few-bit
-values down to fp32's subnormal products) take the FP32 pipe, and operands
-that break a condition (a 25-bit significand, a product below 2^-149, a
-product at 2^128, an Inf, a per-tensor scale) stay on the double-precision
-contraction. Bit-exact against the oracle either way."""
+values down to fp32's subnormal products) take the FP32 pipe (route 1);
+operands that break a condition (a 25-bit significand, a product below
+2^-149, a product at 2^128, an Inf, a per-tensor scale) are scanned and stay
+on the double-precision contraction (route 2); pairwise order, small calls
+and chunk lengths off the k tile never scan (route 0). Bit-exact against the oracle either way."""
 import numpy as np
 import pytest
 
@@ -163,7 +164,7 @@ def test_ineligible_operands_stay_exact(d, case):
         A, _, _ = O.quantize(O.policy(input_format=f, scaling=1), f, 0, x, sa)
     else:
         A = heavy_tailed(rs, M * K)
-    check(d, SEQ, M, N, K, A, K, 1, B, K, 1, route=0)
+    check(d, SEQ, M, N, K, A, K, 1, B, K, 1, route=2)   # scanned, stayed
 
 
 def test_pairwise_and_small_stay_on_double_path(d):
