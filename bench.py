@@ -142,10 +142,8 @@ def cpu_baseline(size: int, budget_s: float, threads: int | None = None):
     rs = np.random.default_rng(0)
     K = size
     cols = min(size, 512)
-    full_a = (rs.standard_normal(size * K, dtype=np.float32) *
-              np.exp(rs.standard_normal(size * K, dtype=np.float32))).astype(np.float64)
-    full_b = (rs.standard_normal(size * K, dtype=np.float32) *
-              np.exp(rs.standard_normal(size * K, dtype=np.float32))).astype(np.float64)
+    full_a = rs.standard_normal(size * K) * np.exp(rs.standard_normal(size * K))
+    full_b = rs.standard_normal(size * K) * np.exp(rs.standard_normal(size * K))
     amax_a, amax_b = O.amax(full_a), O.amax(full_b)
     pols = [O.policy(acc=O.ACC_FP64)]
     for acc in (O.ACC_FP32, O.ACC_FP16, O.ACC_BF16):
@@ -211,11 +209,13 @@ def run_engine(args):
     def make_inputs(seed):
         g = torch.Generator(device=dev)
         g.manual_seed(1000 + seed)
-        x = torch.randn(S, S, device=dev, generator=g, dtype=torch.float32)
-        x *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float32))
-        y = torch.randn(S, S, device=dev, generator=g, dtype=torch.float32)
-        y *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float32))
-        return x.double(), y.double()
+        # Full 53-bit doubles, as Java's nextGaussian gives (the reference's
+        # weights and embeddings start from it).
+        x = torch.randn(S, S, device=dev, generator=g, dtype=torch.float64)
+        x *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float64))
+        y = torch.randn(S, S, device=dev, generator=g, dtype=torch.float64)
+        y *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float64))
+        return x, y
 
     seed = ddist.seeds_for(rank, world, 0)[0]  # this rank's seed, the same every step
     A, B = make_inputs(seed)
@@ -371,7 +371,8 @@ def run_engine(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-        "data": "synthetic: N(0,1) x lognormal(0,1) fp32 values held in doubles, seeded per rank",
+        "data": "synthetic: N(0,1) x lognormal(0,1) doubles (53-bit, like Java's nextGaussian), "
+                "seeded per rank",
         "config": {"workload": f"policy sweep GEMM M=N=K={S}, 12 policies + exact FP64, "
                                f"1 seed per rank per step", "M": M, "N": N, "K": K,
                    "policies": [p.name for p in pols], "seeds_per_step": world, "seed_of_rank_0": 0,
@@ -482,7 +483,7 @@ def run_reference(args):
         # A full step's 13 GEMMs at the sampled rate (each timed step is a bounded row sample).
         "ms_per_step": 13 * float(args.size) ** 3 / value * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "impl": "reference",
-        "data": "synthetic: N(0,1) x lognormal(0,1) fp32 values held in doubles",
+        "data": "synthetic: N(0,1) x lognormal(0,1) doubles (53-bit, like Java's nextGaussian)",
         "config": {"workload": f"policy sweep GEMM M=N=K={args.size}, 12 policies + exact FP64, "
                                f"1 seed per rank per step", "M": args.size, "N": args.size,
                    "K": args.size, "policies": SWEEP_NAMES,
@@ -509,10 +510,11 @@ def run_kernels(args):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev)
     g.manual_seed(1)
-    A = (torch.randn(S, S, device=dev, generator=g) *
-         torch.exp(torch.randn(S, S, device=dev, generator=g))).double()
-    B = (torch.randn(S, S, device=dev, generator=g) *
-         torch.exp(torch.randn(S, S, device=dev, generator=g))).double()
+    f64 = torch.float64
+    A = (torch.randn(S, S, device=dev, generator=g, dtype=f64) *
+         torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=f64)))
+    B = (torch.randn(S, S, device=dev, generator=g, dtype=f64) *
+         torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=f64)))
     C = torch.empty_like(A)
     qA, qB = torch.empty_like(A), torch.empty_like(B)
     scal = torch.zeros((4,), dtype=torch.float64, device=dev)
