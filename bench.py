@@ -234,13 +234,14 @@ def run_engine(args):
     gemm_ms = [0.0] * (n_pol + 1)
     launches = [0]
     # Each contraction's route (drift_gemm_route), read in the first warm-up
-    # step: route 0 is one launch; routes 1 (FP32 pipe) and 2 (scanned, stayed
-    # on the double-precision kernel) are five (two operand scans, the
-    # decision, and both contractions, one of which stands down at once).
+    # step: routes 0 (tiled) and 3 (one output per thread) are one launch;
+    # routes 1 (FP32 pipe) and 2 (scanned, stayed on the double-precision
+    # kernels) are five (two operand scans, the decision, and both
+    # contractions, one of which stands down at once).
     routes = [None] * (n_pol + 1)
 
     def gemm_launches(k):
-        return 1 if not routes[k] else 5
+        return 5 if routes[k] in (d.ROUTE_FP32, d.ROUTE_SCANNED) else 1
 
     def cast(p, src, dst, slot, counter):
         f = p.input_format

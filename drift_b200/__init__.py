@@ -12,7 +12,8 @@ from .fmt import Formats, MiniFloat, Rng, Rounding, Specials
 from .kernel import (Acc, Dot, NumericPolicy, Order, Quant, Scaling, Window, amax_dev,
                      check_dev, contract, contract_dev, contraction, error_sums_dev, gemm,
                      per_tensor_scale_dev, probe_fp32, probe_fp64, gemm_dev, gemm_route,
-                     quantize_dev, ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED)
+                     quantize_dev, set_thin_tiles, ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED,
+                     ROUTE_STAGED)
 from . import policies
 
 _lib.load()
@@ -20,5 +21,5 @@ _lib.load()
 __all__ = ["Context", "DriftError", "Formats", "MiniFloat", "Rng", "Rounding", "Specials", "Acc",
            "Dot", "NumericPolicy", "Order", "Quant", "Scaling", "Window", "contraction", "contract",
            "contract_dev", "gemm", "gemm_dev", "gemm_route", "quantize_dev", "ROUTE_DOUBLE",
-           "ROUTE_FP32", "ROUTE_SCANNED",
+           "ROUTE_FP32", "ROUTE_SCANNED", "ROUTE_STAGED", "set_thin_tiles",
            "amax_dev", "check_dev", "policies"]

@@ -153,6 +153,7 @@ struct drift_ctx {
     unsigned long long *d_clamped() { return (unsigned long long *)(d_small + 16); }
     double *d_scalar() { return (double *)(d_small + 24); }
     int *d_route() { return (int *)(d_small + 32); }
+    int64_t thin_tiles = -1;  // drift_set_thin_tiles; negative: two per SM
 };
 
 static int enter(drift_ctx *ctx) {
@@ -603,8 +604,8 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
                 break;
             }
             rc = launch_gemm(ctx->ws, ctx->sched, p, rows, N, K, d_a + off, a_row_stride, 1, d_b,
-                             b_row_stride, b_k_stride, d_bias, d_c + r0 * N, N, ctx->d_err(),
-                             ctx->d_route(), st);
+                             b_row_stride, b_k_stride, d_bias, d_c + r0 * N, N, ctx->thin_tiles,
+                             ctx->d_err(), ctx->d_route(), st);
             if (rc) {
                 rc = fail(rc, "gemm launch");
                 break;
@@ -631,7 +632,8 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
                              ctx->d_state(), ctx->d_err(), st);
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
-                         b_row_stride, b_k_stride, d_bias, d_c, N, ctx->d_err(), ctx->d_route(), st);
+                         b_row_stride, b_k_stride, d_bias, d_c, N, ctx->thin_tiles, ctx->d_err(),
+                         ctx->d_route(), st);
     }
     if (rc) return fail(rc, "gemm launch");
     CUDA_TRY(cudaMemcpy2DAsync(C, c_row_stride * 8, d_c, N * 8, N * 8, M, cudaMemcpyDeviceToHost, st),
@@ -727,10 +729,17 @@ int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, 
                              d_rng_state, ctx->d_err(), pick(ctx, stream));
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
-                         b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->d_err(),
-                         ctx->d_route(), pick(ctx, stream));
+                         b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->thin_tiles,
+                         ctx->d_err(), ctx->d_route(), pick(ctx, stream));
     }
     return rc ? fail(rc, "gemm launch") : DRIFT_OK;
+}
+
+int drift_set_thin_tiles(drift_ctx *ctx, int64_t tiles) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    ctx->thin_tiles = tiles < 0 ? -1 : tiles;
+    return DRIFT_OK;
 }
 
 int drift_gemm_route(drift_ctx *ctx, int *route, void *stream) {

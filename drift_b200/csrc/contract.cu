@@ -55,6 +55,8 @@ struct ContractArgs {
     const uint64_t *state;   // Rng state before the first draw (stochastic only)
     const int64_t *offsets;  // first draw index of each dot, (t, i, o) order
     uint32_t *counts;        // draws each dot made
+    const int *skip;         // staged kernel: leave at once if this word is nonzero
+    int *route;              // staged kernel: receives DRIFT_ROUTE_STAGED when given
 };
 
 __device__ __forceinline__ void window_of(const ContractArgs &g, int64_t i, int64_t &lo,
@@ -349,6 +351,49 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
     g.counts[out] = rnd.cnt;
 }
 
+// One output per thread over a FULL window with nearest or truncating
+// accumulation, the operands staged CTA-wide in 32-term chunks as above: the
+// route for contractions whose outputs are too few to fill the GPU with the
+// tiled kernel's 64 x 64 tiles (a batch-64 linear layer gives 32 of them, so
+// 32 SMs each ran sixteen 2048-long chains per thread while the rest idled).
+template <int ACC, int RM>
+__global__ void __launch_bounds__(kStageSide *kStageSide)
+    contract_staged_kernel(const ContractArgs g) {
+    if (g.skip && *g.skip) return;  // the FP32 pipe (gemm32.cu) took the call
+    if (g.route && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0)
+        *g.route = DRIFT_ROUTE_STAGED;
+    __shared__ double sA[kStageSide][kStageK + 1], sB[kStageSide][kStageK + 1];
+    const int tx = threadIdx.x % kStageSide, ty = threadIdx.x / kStageSide;
+    const int64_t t = blockIdx.z;
+    const int64_t i0 = (int64_t)blockIdx.y * kStageSide, o0 = (int64_t)blockIdx.x * kStageSide;
+    const int64_t i = i0 + ty, o = o0 + tx;
+    const bool live = i < g.rows && o < g.cols;
+    const double *At = g.A + t * g.a_batch, *Bt = g.B + t * g.b_batch;
+    int64_t k0 = -kStageK;
+    auto stage = [&](int64_t base) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < kStageSide * kStageK; e += kStageSide * kStageSide) {
+            const int r = e / kStageK, c = e % kStageK;
+            const int64_t k = base + c;
+            const bool kin = k < g.depth;
+            sA[r][c] = (kin && i0 + r < g.rows) ? __ldg(At + (i0 + r) * g.a_row + k * g.a_k) : 0.0;
+            sB[r][c] = (kin && o0 + r < g.cols) ? __ldg(Bt + (o0 + r) * g.b_col + k * g.b_k) : 0.0;
+        }
+        __syncthreads();
+        k0 = base;
+    };
+    auto term = [&](int64_t k) {
+        if (k < k0 || k >= k0 + kStageK) stage(k - k % kStageK);  // the same k in every thread
+        return __dmul_rn(sA[ty][k - k0], sB[tx][k - k0]);
+    };
+    ExactRounder<ACC, RM> rnd;
+    const double v = dot_terms<ACC>(g, term, g.depth, rnd);
+    if (!live) return;
+    double *c = g.C + t * g.c_batch + i * g.c_row + o * g.c_col;
+    if (g.causal && o > i) *c = 0.0;
+    else store(g, c, o, v);
+}
+
 // The dots in order, one thread: the fallback that is correct for any data.
 template <int ACC>
 __global__ void contract_sr_serial_kernel(const ContractArgs g, double *vals,
@@ -552,6 +597,39 @@ static bool tiled_route(const ContractDesc &d) {
            op.batch <= 65535 && (op.rows + 63) / 64 <= 65535 && op.c_row >= op.cols &&
            op.a_batch >= 0 && op.a_row >= 0 && op.a_k >= 0 && op.b_batch >= 0 && op.b_col >= 0 &&
            op.b_k >= 0 && op.c_batch >= 0;
+}
+
+int launch_contract_staged(const drift_policy *p, const ContractDesc &d, const int *skip,
+                           int *route, cudaStream_t st) {
+    const drift_contraction &op = d.op;
+    if (op.window != DRIFT_WINDOW_FULL || stochastic(p) || op.batch > 65535 ||
+        (op.rows + kStageSide - 1) / kStageSide > 65535 ||
+        (op.cols + kStageSide - 1) / kStageSide > 0x7fffffffLL)
+        return DRIFT_EINVAL;
+    if (op.batch * op.rows * op.cols == 0) return DRIFT_OK;
+    ContractArgs g = args_of(p, d);
+    g.skip = skip;
+    g.route = route;
+    const dim3 grid((unsigned)((op.cols + kStageSide - 1) / kStageSide),
+                    (unsigned)((op.rows + kStageSide - 1) / kStageSide), (unsigned)op.batch);
+    const unsigned threads = kStageSide * kStageSide;
+    const bool tr = p->acc_rounding == DRIFT_TRUNCATE;
+    switch (p->acc) {
+        case DRIFT_ACC_FP64:
+            contract_staged_kernel<DRIFT_ACC_FP64, DRIFT_NEAREST_EVEN><<<grid, threads, 0, st>>>(g);
+            break;
+        case DRIFT_ACC_FP32:
+            contract_staged_kernel<DRIFT_ACC_FP32, DRIFT_NEAREST_EVEN><<<grid, threads, 0, st>>>(g);
+            break;
+        case DRIFT_ACC_FP16:
+            if (tr) contract_staged_kernel<DRIFT_ACC_FP16, DRIFT_TRUNCATE><<<grid, threads, 0, st>>>(g);
+            else contract_staged_kernel<DRIFT_ACC_FP16, DRIFT_NEAREST_EVEN><<<grid, threads, 0, st>>>(g);
+            break;
+        default:
+            if (tr) contract_staged_kernel<DRIFT_ACC_BF16, DRIFT_TRUNCATE><<<grid, threads, 0, st>>>(g);
+            else contract_staged_kernel<DRIFT_ACC_BF16, DRIFT_NEAREST_EVEN><<<grid, threads, 0, st>>>(g);
+    }
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 
 int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,

@@ -562,18 +562,53 @@ static int gemm_batched(ScheduleCache &cache, const drift_policy *p, int64_t bat
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
-                int *d_err, int *d_route, cudaStream_t st) {
+                int64_t thin_tiles, int *d_err, int *d_route, cudaStream_t st) {
     if (M < 0 || N < 0 || K < 0 || a_rs < 0 || a_ks < 0 || b_rs < 0 || b_ks < 0 || c_rs < 0 ||
         p->acc < 0 || p->acc > 3 || p->order < 0 || p->order > 3)
         return DRIFT_EINVAL;
+    if (M == 0 || N == 0) return DRIFT_OK;
     // FP32 accumulation over narrow products may go to the FP32 pipe; the
-    // decision is made on the device, and this launch stands down if taken.
+    // decision is made on the device, and the launch below stands down if taken.
     const int *skip = nullptr;
     int rc = launch_gemm_f32(ws, p, M, N, K, A, a_rs, a_ks, B, b_rs, b_ks, bias, C, c_rs, d_err,
                              d_route, st, &skip);
     if (rc) return rc;
-    if (!skip && d_route && cudaMemsetAsync(d_route, 0, sizeof(int), st) != cudaSuccess)
-        return DRIFT_ECUDA;
+    // Too few 64 x 64 tiles to occupy the GPU: one output per thread instead,
+    // so that every SM has chains to run. A batch-64 linear layer of 2048
+    // outputs is 32 tiles, which left 116 of 148 SMs idle while each busy
+    // thread ran sixteen chains. Measured on one B200, one output per thread
+    // won for the rounding accumulators at 32 tiles (1.3-1.6x at K = 2048) and
+    // 2 tiles (4-6.6x), lost at 64 tiles (1.1-1.4x), and never won for FP64,
+    // whose bare-add chains the tiles' sixteen-way interleave keeps fed. So by
+    // default only FP32/FP16/BF16 calls under a quarter tile per SM go there;
+    // an explicit threshold applies to every accumulator.
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const bool thin = thin_tiles < 0
+                          ? p->acc != DRIFT_ACC_FP64 && tiles < std::max(1, sm_count() / 4)
+                          : tiles < thin_tiles;
+    const bool staged = thin && (M + 15) / 16 <= 65535;
+    if (!skip && !staged && d_route && cudaMemsetAsync(d_route, 0, sizeof(int), st) != cudaSuccess)
+        return DRIFT_ECUDA;  // DRIFT_ROUTE_DOUBLE
+    if (staged) {
+        ContractDesc d{};
+        d.op.batch = 1;
+        d.op.rows = M;
+        d.op.cols = N;
+        d.op.depth = K;
+        d.op.a_row = a_rs;
+        d.op.a_k = a_ks;
+        d.op.b_col = b_rs;
+        d.op.b_k = b_ks;
+        d.op.c_row = c_rs;
+        d.op.c_col = 1;
+        d.op.alpha = 1.0;
+        d.op.window = DRIFT_WINDOW_FULL;
+        d.a = A;
+        d.b = B;
+        d.c = C;
+        d.bias = bias;
+        return launch_contract_staged(p, d, skip, skip ? nullptr : d_route, st);
+    }
     return gemm_batched(cache, p, 1, M, N, K, A, a_rs, a_ks, 0, B, b_rs, b_ks, 0, bias, C, c_rs, 0,
                         d_err, skip, st);
 }

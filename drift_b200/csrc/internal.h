@@ -85,6 +85,13 @@ struct ContractDesc {
     const double *bias;
 };
 int check_contraction(const drift_contraction &op);
+// A FULL-window, non-stochastic contraction with one output per thread and
+// the operands staged in shared memory (contract.cu): the launch for calls
+// whose outputs are too few for the tiled kernel to fill the GPU. It stands
+// down at once if `skip` is given and reads nonzero; `route`, when given,
+// receives DRIFT_ROUTE_STAGED.
+int launch_contract_staged(const drift_policy *p, const ContractDesc &d, const int *skip,
+                           int *route, cudaStream_t st);
 int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
                     const ContractDesc &d, uint64_t *d_state, int *d_err, cudaStream_t st);
 // A batch of `batch` contractions, problem z at A + z*a_bs, B + z*b_bs,
@@ -96,12 +103,14 @@ int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy 
                         int *d_err, cudaStream_t st);
 int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
 int launch_fp32_probe(cudaStream_t st, double *fma_per_s);
-// One contraction C = A B^T (+ bias). `d_route`, when given, receives 1 if
-// the call ran on the FP32 pipe (gemm32.cu) and 0 otherwise.
+// One contraction C = A B^T (+ bias). `d_route`, when given, receives the
+// DRIFT_ROUTE_* of the path taken.
+// Calls with fewer 64 x 64 output tiles than `thin_tiles` run one output per
+// thread (launch_contract_staged); a negative value means two per SM.
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
-                int *d_err, int *d_route, cudaStream_t st);
+                int64_t thin_tiles, int *d_err, int *d_route, cudaStream_t st);
 // gemm32.cu: queues the FP32-pipe path of an FP32-accumulated contraction
 // whose policy and shape qualify (an operand scan, a device-side decision and
 // the FFMA contraction, which stands down unless the scan allows it). Sets

@@ -403,19 +403,29 @@ def error_sums_dev(got, exact, d_sums, *, stream=None, ctx=None) -> None:
                                                 got.numel(), _tptr(d_sums), _stream_ptr(stream)))
 
 
-ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED = 0, 1, 2
+ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED, ROUTE_STAGED = 0, 1, 2, 3
 
 
 def gemm_route(stream=None, ctx=None) -> int:
     """The path of the context's last non-stochastic GEMM: ROUTE_FP32 for the
     FP32 pipe (narrow products under an FP32 accumulator), ROUTE_SCANNED for a
     candidate whose operands kept it on the double-precision contraction,
-    ROUTE_DOUBLE for the double-precision contraction alone. Synchronises the
-    stream."""
+    ROUTE_STAGED for one output per thread (a call too thin to fill the GPU
+    with 64 x 64 tiles), ROUTE_DOUBLE for the tiled double-precision
+    contraction alone. Synchronises the stream."""
     ctx = ctx or _lib.Context.current()
     out = ctypes.c_int()
     _lib.check(_lib.load().drift_gemm_route(ctx.handle, ctypes.byref(out), _stream_ptr(stream)))
     return out.value
+
+
+def set_thin_tiles(tiles: int, ctx=None) -> None:
+    """GEMM calls with fewer than `tiles` 64 x 64 output tiles run one output
+    per thread (ROUTE_STAGED); negative restores the default (FP32/FP16/BF16
+    calls under a quarter tile per SM, FP64 never), 0 sends every call to the
+    tiled kernel. Results do not change."""
+    ctx = ctx or _lib.Context.current()
+    _lib.check(_lib.load().drift_set_thin_tiles(ctx.handle, int(tiles)))
 
 
 def probe_fp64(ctx=None) -> float:

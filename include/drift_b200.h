@@ -319,14 +319,27 @@ DRIFT_API int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
  *                          product of the two operands an exact fp32 number,
  *                          so that Dot.java's (float)(s + a*b) is one fp32 FMA;
  *   DRIFT_ROUTE_SCANNED  2  a candidate for the FP32 pipe whose operand scan
- *                          kept it on the double-precision contraction.
+ *                          kept it on the double-precision contraction;
+ *   DRIFT_ROUTE_STAGED   3  one output per thread with the operands staged in
+ *                          shared memory (one launch): a call too thin for
+ *                          the tiled kernel (drift_set_thin_tiles).
  * Every route gives the same bits; the route is a performance fact (routes 1
  * and 2 launch five kernels: two scans, the decision and both contractions,
  * one of which stands down). Waits for `stream`. */
 #define DRIFT_ROUTE_DOUBLE 0
 #define DRIFT_ROUTE_FP32 1
 #define DRIFT_ROUTE_SCANNED 2
+#define DRIFT_ROUTE_STAGED 3
 DRIFT_API int drift_gemm_route(drift_ctx *ctx, int *route, void *stream);
+
+/* No counterpart in the reference (a tuning knob; results do not change):
+ * drift_gemm / drift_gemm_dev calls whose M x N outputs make fewer than
+ * `tiles` 64 x 64 tiles run one output per thread instead of on the tiled
+ * kernel, so that a thin call (a batch-64 linear layer) still reaches every
+ * SM. Negative restores the default: FP32/FP16/BF16 accumulators below a
+ * quarter tile per SM (37 tiles on a B200), FP64 never. 0 sends every call
+ * to the tiled kernel. */
+DRIFT_API int drift_set_thin_tiles(drift_ctx *ctx, int64_t tiles);
 
 /* Error sums of RealDotSweep's RMS ratio
  * (java/.../tools/RealDotSweep.java:245-257): ADDS sum((got-exact)^2) to

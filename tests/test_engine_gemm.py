@@ -1,5 +1,6 @@
 """GPU parity of the contraction: Dot.dot over whole GEMMs, every accumulator
-width, order and accumulator rounding, the three layouts of Pass.java
+width, order and accumulator rounding, on both double-precision routes (the
+tiled kernel and one output per thread), the three layouts of Pass.java
 (forward NT, dgrad with a strided W column, wgrad with both operands strided),
 offsets, bias, and the values that leave the integer fast path (zeros,
 cancellation to -0.0, subnormal sums, overflow, saturation). Bit-exact
@@ -22,6 +23,19 @@ def d():
     return drift_b200
 
 
+EXPECT_ROUTE = [None]
+
+
+@pytest.fixture(scope="module", params=["tiled", "staged"], autouse=True)
+def kernel_route(request, d):
+    """Every case runs twice: on the tiled kernel (thin-call threshold 0) and
+    with one output per thread (a threshold above any call here)."""
+    d.set_thin_tiles(0 if request.param == "tiled" else 1 << 40)
+    EXPECT_ROUTE[0] = d.ROUTE_DOUBLE if request.param == "tiled" else d.ROUTE_STAGED
+    yield request.param
+    d.set_thin_tiles(-1)
+
+
 def policies(d):
     for acc in ACCS:
         for order in ORDERS:
@@ -34,6 +48,7 @@ def compare(d, acc, order, rm, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_
     p = (d.NumericPolicy.builder("t").acc(d.Acc(acc)).order(d.Order(order))
          .acc_rounding(d.Rounding(rm)).acc_block(acc_block).build())
     got = d.gemm(p, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks, bias=bias)
+    assert d.gemm_route() == EXPECT_ROUTE[0]
     op = O.policy(acc=acc, order=order, acc_rounding=rm, acc_block=acc_block)
     want, _ = O.gemm(op, M, N, K, A, a_off, a_rs, a_ks, B, b_off, b_rs, b_ks, bias=bias, threads=8)
     assert_bits(got, want, f"acc={acc} order={order} rm={rm} M={M} N={N} K={K}")

@@ -9,7 +9,8 @@ values down to fp32's subnormal products) take the FP32 pipe (route 1);
 operands that break a condition (a 25-bit significand, a product below
 2^-149, a product at 2^128, an Inf, a per-tensor scale) are scanned and stay
 on the double-precision contraction (route 2); pairwise order, small calls
-and chunk lengths off the k tile never scan (route 0). Bit-exact against the oracle either way."""
+and chunk lengths off the k tile never scan (route 0 tiled, or 3 for a call
+too thin for the tiles). Bit-exact against the oracle either way."""
 import numpy as np
 import pytest
 
@@ -171,9 +172,19 @@ def test_pairwise_and_small_stay_on_double_path(d):
     rs = np.random.default_rng(17)
     A = bf16_cast(heavy_tailed(rs, 512 * 512))
     B = bf16_cast(heavy_tailed(rs, 512 * 512))
+    # Forced to one output per thread (route 3), then to the tiled kernel.
+    for thin, r in ((1 << 40, 3), (0, 0)):
+        d.set_thin_tiles(thin)
+        try:
+            check(d, PAIR, 512, 512, 512, A, 512, 1, B, 512, 1, route=r)
+            check(d, SEQ, 256, 256, 256, A, 256, 1, B, 256, 1, route=r)  # below 2^27 MACs
+            check(d, BLOCK, 512, 512, 512, A, 512, 1, B, 512, 1, route=r, blk=40)  # chunk off-tile
+        finally:
+            d.set_thin_tiles(-1)
+    # By default 512 x 512 outputs (64 tiles of 64 x 64) stay tiled and
+    # 256 x 256 (16 tiles) go one output per thread.
     check(d, PAIR, 512, 512, 512, A, 512, 1, B, 512, 1, route=0)
-    check(d, SEQ, 256, 256, 256, A, 256, 1, B, 256, 1, route=0)     # below 2^27 MACs
-    check(d, BLOCK, 512, 512, 512, A, 512, 1, B, 512, 1, route=0, blk=40)  # chunk not k-tiled
+    check(d, SEQ, 256, 256, 256, A, 256, 1, B, 256, 1, route=3)
 
 
 def test_pipelined_host_call_chunks(d):
