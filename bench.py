@@ -508,15 +508,16 @@ def run_kernels(args):
     import drift_b200 as d
 
     S = args.size
+    M, N, K = (int(x) for x in args.mnk.split(",")) if args.mnk else (S, S, S)
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev)
     g.manual_seed(1)
     f64 = torch.float64
-    A = (torch.randn(S, S, device=dev, generator=g, dtype=f64) *
-         torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=f64)))
-    B = (torch.randn(S, S, device=dev, generator=g, dtype=f64) *
-         torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=f64)))
-    C = torch.empty_like(A)
+    A = (torch.randn(M, K, device=dev, generator=g, dtype=f64) *
+         torch.exp(torch.randn(M, K, device=dev, generator=g, dtype=f64)))
+    B = (torch.randn(N, K, device=dev, generator=g, dtype=f64) *
+         torch.exp(torch.randn(N, K, device=dev, generator=g, dtype=f64)))
+    C = torch.empty((M, N), dtype=f64, device=dev)
     qA, qB = torch.empty_like(A), torch.empty_like(B)
     scal = torch.zeros((4,), dtype=torch.float64, device=dev)
     pols = [d.NumericPolicy.exact()] + sweep_policies(d)
@@ -547,10 +548,10 @@ def run_kernels(args):
                 d.gemm_dev(p, a, b, C)
             e1.record(stream)
             torch.cuda.synchronize()
-            out[p.name] = args.steps * S ** 3 / (e0.elapsed_time(e1) * 1e-3)
+            out[p.name] = args.steps * M * N * K / (e0.elapsed_time(e1) * 1e-3)
     d.check_dev()
-    print(json.dumps({"mode": "kernels", "size": S, "mac_per_s": out, "routes": routes}),
-          flush=True)
+    print(json.dumps({"mode": "kernels", "M": M, "N": N, "K": K, "mac_per_s": out,
+                      "routes": routes}), flush=True)
     return 0
 
 
@@ -715,6 +716,7 @@ def main() -> int:
     ap.add_argument("--mode", choices=["sweep", "kernels", "train", "configs"], default="sweep",
                     help="kernels: time each policy's contraction alone (for profiling)")
     ap.add_argument("--policies", default="", help="kernels mode: comma-separated policy names")
+    ap.add_argument("--mnk", default="", help="kernels mode: M,N,K instead of size^3")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "engine":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)

@@ -382,12 +382,55 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
         __syncthreads();
         k0 = base;
     };
-    auto term = [&](int64_t k) {
-        if (k < k0 || k >= k0 + kStageK) stage(k - k % kStageK);  // the same k in every thread
-        return __dmul_rn(sA[ty][k - k0], sB[tx][k - k0]);
-    };
     ExactRounder<ACC, RM> rnd;
-    const double v = dot_terms<ACC>(g, term, g.depth, rnd);
+    auto step = [&](double acc, double a, double b) {  // Dot.forward's add (:46, :54, :63)
+        const double t = __dadd_rn(acc, __dmul_rn(a, b));
+        return ACC == DRIFT_ACC_FP64 ? t : rnd(t);
+    };
+    double v;
+    if (g.order == DRIFT_SEQUENTIAL || g.order == DRIFT_REVERSED ||
+        (g.order == DRIFT_BLOCKED && g.acc_block % kStageK == 0)) {
+        // One staged chunk at a time with a fixed 32-term body: the chunk
+        // walk of Dot.forward / backward, and of Dot.blocked when its chunks
+        // end on chunk edges. (The per-term window check of the general walk
+        // below cost 34 instructions per multiply-accumulate, against about 10
+        // here.)
+        const bool rev = g.order == DRIFT_REVERSED, blk = g.order == DRIFT_BLOCKED;
+        const int64_t nch = (g.depth + kStageK - 1) / kStageK;
+        const int64_t fold_every = blk ? g.acc_block / kStageK : 0;
+        double acc = 0.0, total = 0.0;
+        for (int64_t c = 0; c < nch; c++) {
+            const int64_t cc = rev ? nch - 1 - c : c;
+            stage(cc * kStageK);
+            const double *ra = sA[ty], *rb = sB[tx];
+            const int64_t rest = g.depth - cc * kStageK;
+            const int len = rest < kStageK ? (int)rest : kStageK;
+            if (len == kStageK && !rev) {
+#pragma unroll 8
+                for (int q = 0; q < kStageK; q++) acc = step(acc, ra[q], rb[q]);
+            } else if (len == kStageK) {
+#pragma unroll 8
+                for (int q = kStageK - 1; q >= 0; q--) acc = step(acc, ra[q], rb[q]);
+            } else if (!rev) {
+                for (int q = 0; q < len; q++) acc = step(acc, ra[q], rb[q]);
+            } else {
+                for (int q = len - 1; q >= 0; q--) acc = step(acc, ra[q], rb[q]);
+            }
+            if (blk && ((c + 1) % fold_every == 0 || c == nch - 1)) {  // Dot.blocked (:115-118)
+                total = ACC == DRIFT_ACC_FP64
+                            ? __dadd_rn(total, acc)
+                            : (double)__double2float_rn(__dadd_rn(total, acc));
+                acc = 0.0;
+            }
+        }
+        v = blk ? total : acc;
+    } else {
+        auto term = [&](int64_t k) {
+            if (k < k0 || k >= k0 + kStageK) stage(k - k % kStageK);  // the same k in every thread
+            return __dmul_rn(sA[ty][k - k0], sB[tx][k - k0]);
+        };
+        v = dot_terms<ACC>(g, term, g.depth, rnd);
+    }
     if (!live) return;
     double *c = g.C + t * g.c_batch + i * g.c_row + o * g.c_col;
     if (g.causal && o > i) *c = 0.0;
@@ -597,6 +640,19 @@ static bool tiled_route(const ContractDesc &d) {
            op.batch <= 65535 && (op.rows + 63) / 64 <= 65535 && op.c_row >= op.cols &&
            op.a_batch >= 0 && op.a_row >= 0 && op.a_k >= 0 && op.b_batch >= 0 && op.b_col >= 0 &&
            op.b_k >= 0 && op.c_batch >= 0;
+}
+
+int64_t staged_tile_limit(const drift_policy *p) {
+    // Measured on one B200 (tiled time / staged time, K = 512-2048): at 32
+    // tiles of 64 x 64 the staged kernel won everywhere (FP64 1.29, pairwise
+    // 1.27, the chunk walks with a rounding accumulator 2.0-2.6); at 64 tiles
+    // only the chunk walks still won (1.24-1.5; FP64 0.8, pairwise 0.7); at
+    // 128 none did (0.4-0.86).
+    const bool chunk_walk = p->order == DRIFT_SEQUENTIAL || p->order == DRIFT_REVERSED ||
+                            (p->order == DRIFT_BLOCKED && std::max<int64_t>(1, p->acc_block) %
+                                                             kStageK == 0);
+    const int64_t sms = sm_count();
+    return chunk_walk && p->acc != DRIFT_ACC_FP64 ? 2 * sms / 3 : sms / 3;
 }
 
 int launch_contract_staged(const drift_policy *p, const ContractDesc &d, const int *skip,

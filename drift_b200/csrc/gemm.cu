@@ -576,16 +576,10 @@ int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int6
     // Too few 64 x 64 tiles to occupy the GPU: one output per thread instead,
     // so that every SM has chains to run. A batch-64 linear layer of 2048
     // outputs is 32 tiles, which left 116 of 148 SMs idle while each busy
-    // thread ran sixteen chains. Measured on one B200, one output per thread
-    // won for the rounding accumulators at 32 tiles (1.3-1.6x at K = 2048) and
-    // 2 tiles (4-6.6x), lost at 64 tiles (1.1-1.4x), and never won for FP64,
-    // whose bare-add chains the tiles' sixteen-way interleave keeps fed. So by
-    // default only FP32/FP16/BF16 calls under a quarter tile per SM go there;
-    // an explicit threshold applies to every accumulator.
+    // thread ran sixteen chains. The default limit depends on the policy
+    // (staged_tile_limit, measured); an explicit one applies to every call.
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-    const bool thin = thin_tiles < 0
-                          ? p->acc != DRIFT_ACC_FP64 && tiles < std::max(1, sm_count() / 4)
-                          : tiles < thin_tiles;
+    const bool thin = tiles < (thin_tiles < 0 ? staged_tile_limit(p) : thin_tiles);
     const bool staged = thin && (M + 15) / 16 <= 65535;
     if (!skip && !staged && d_route && cudaMemsetAsync(d_route, 0, sizeof(int), st) != cudaSuccess)
         return DRIFT_ECUDA;  // DRIFT_ROUTE_DOUBLE

@@ -92,6 +92,9 @@ int check_contraction(const drift_contraction &op);
 // receives DRIFT_ROUTE_STAGED.
 int launch_contract_staged(const drift_policy *p, const ContractDesc &d, const int *skip,
                            int *route, cudaStream_t st);
+// The default thin-call limit of a policy: GEMMs with fewer 64 x 64 output
+// tiles run on launch_contract_staged.
+int64_t staged_tile_limit(const drift_policy *p);
 int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
                     const ContractDesc &d, uint64_t *d_state, int *d_err, cudaStream_t st);
 // A batch of `batch` contractions, problem z at A + z*a_bs, B + z*b_bs,

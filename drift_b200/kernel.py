@@ -421,9 +421,10 @@ def gemm_route(stream=None, ctx=None) -> int:
 
 def set_thin_tiles(tiles: int, ctx=None) -> None:
     """GEMM calls with fewer than `tiles` 64 x 64 output tiles run one output
-    per thread (ROUTE_STAGED); negative restores the default (FP32/FP16/BF16
-    calls under a quarter tile per SM, FP64 never), 0 sends every call to the
-    tiled kernel. Results do not change."""
+    per thread (ROUTE_STAGED); negative restores the default (measured per
+    policy: under two thirds of a tile per SM for sequential, reversed and
+    32-aligned blocked orders with a rounding accumulator, a third otherwise),
+    0 sends every call to the tiled kernel. Results do not change."""
     ctx = ctx or _lib.Context.current()
     _lib.check(_lib.load().drift_set_thin_tiles(ctx.handle, int(tiles)))
 

@@ -336,9 +336,10 @@ DRIFT_API int drift_gemm_route(drift_ctx *ctx, int *route, void *stream);
  * drift_gemm / drift_gemm_dev calls whose M x N outputs make fewer than
  * `tiles` 64 x 64 tiles run one output per thread instead of on the tiled
  * kernel, so that a thin call (a batch-64 linear layer) still reaches every
- * SM. Negative restores the default: FP32/FP16/BF16 accumulators below a
- * quarter tile per SM (37 tiles on a B200), FP64 never. 0 sends every call
- * to the tiled kernel. */
+ * SM. Negative restores the default, measured per policy: below two thirds
+ * of a tile per SM (98 tiles on a B200) for sequential, reversed and
+ * 32-aligned blocked orders with an FP32/FP16/BF16 accumulator, below a third
+ * (49) otherwise. 0 sends every call to the tiled kernel. */
 DRIFT_API int drift_set_thin_tiles(drift_ctx *ctx, int64_t tiles);
 
 /* Error sums of RealDotSweep's RMS ratio

@@ -126,7 +126,7 @@ def test_pairwise_trees_regular_and_irregular(d, acc, K):
 
 
 @pytest.mark.parametrize("acc", ACCS)
-@pytest.mark.parametrize("acc_block", [1, 7, 32, 37, 1000])
+@pytest.mark.parametrize("acc_block", [1, 7, 32, 37, 64, 96, 1000])
 def test_blocked_any_chunk(d, acc, acc_block):
     rs = np.random.default_rng(acc_block)
     M, N, K = 5, 70, 300

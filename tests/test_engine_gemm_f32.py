@@ -181,8 +181,8 @@ def test_pairwise_and_small_stay_on_double_path(d):
             check(d, BLOCK, 512, 512, 512, A, 512, 1, B, 512, 1, route=r, blk=40)  # chunk off-tile
         finally:
             d.set_thin_tiles(-1)
-    # By default 512 x 512 outputs (64 tiles of 64 x 64) stay tiled and
-    # 256 x 256 (16 tiles) go one output per thread.
+    # By default pairwise over 512 x 512 outputs (64 tiles of 64 x 64) stays
+    # tiled, and sequential over 256 x 256 (16 tiles) goes one output per thread.
     check(d, PAIR, 512, 512, 512, A, 512, 1, B, 512, 1, route=0)
     check(d, SEQ, 256, 256, 256, A, 256, 1, B, 256, 1, route=3)
 
