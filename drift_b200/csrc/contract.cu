@@ -405,12 +405,38 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
             const double *ra = sA[ty], *rb = sB[tx];
             const int64_t rest = g.depth - cc * kStageK;
             const int len = rest < kStageK ? (int)rest : kStageK;
-            if (len == kStageK && !rev) {
-#pragma unroll 8
-                for (int q = 0; q < kStageK; q++) acc = step(acc, ra[q], rb[q]);
-            } else if (len == kStageK) {
-#pragma unroll 8
-                for (int q = kStageK - 1; q >= 0; q--) acc = step(acc, ra[q], rb[q]);
+            if (len == kStageK) {
+                // Eight steps at a time on the fast rounding with one range
+                // check for the eight; a miss redoes them exactly from the
+                // sum before them (as the tiled kernel's groups do across
+                // outputs): every fast result that passes is the exact one.
+#pragma unroll 1
+                for (int q0 = 0; q0 < kStageK; q0 += 8) {
+                    double pr[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int q = rev ? kStageK - 1 - (q0 + j) : q0 + j;
+                        pr[j] = __dmul_rn(ra[q], rb[q]);
+                    }
+                    if constexpr (ACC == DRIFT_ACC_FP64) {
+#pragma unroll
+                        for (int j = 0; j < 8; j++) acc = __dadd_rn(acc, pr[j]);
+                    } else {
+                        using R = AccRound<ACC, RM>;
+                        const double s0 = acc;
+                        bool ok = true;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            acc = R::fast(__dadd_rn(acc, pr[j]));
+                            ok = ok & R::ok(acc);
+                        }
+                        if (!ok) {
+                            acc = s0;
+#pragma unroll
+                            for (int j = 0; j < 8; j++) acc = R::exact(__dadd_rn(acc, pr[j]));
+                        }
+                    }
+                }
             } else if (!rev) {
                 for (int q = 0; q < len; q++) acc = step(acc, ra[q], rb[q]);
             } else {
