@@ -351,11 +351,21 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
     g.counts[out] = rnd.cnt;
 }
 
-// One output per thread over a FULL window with nearest or truncating
-// accumulation, the operands staged CTA-wide in 32-term chunks as above: the
-// route for contractions whose outputs are too few to fill the GPU with the
+// Orders the staged kernel walks chunk by chunk with a fixed body: the
+// sequential and reversed chains over any window, and blocked chains whose
+// blocks end on 32-term chunk edges when every window starts at term 0.
+__host__ __device__ inline bool staged_walk(int order, int64_t acc_block, int window) {
+    return order == DRIFT_SEQUENTIAL || order == DRIFT_REVERSED ||
+           (order == DRIFT_BLOCKED && acc_block % kStageK == 0 && window != DRIFT_WINDOW_SUFFIX);
+}
+
+// One output per thread with nearest or truncating accumulation, the
+// operands staged CTA-wide in 32-term chunks as above. Two routes use it:
+// FULL-window contractions whose outputs are too few to fill the GPU with the
 // tiled kernel's 64 x 64 tiles (a batch-64 linear layer gives 32 of them, so
-// 32 SMs each ran sixteen 2048-long chains per thread while the rest idled).
+// 32 SMs each ran sixteen 2048-long chains per thread while the rest idled),
+// and the ragged PREFIX / SUFFIX windows of the attention matmuls in the
+// orders it walks chunk by chunk (staged_walk).
 template <int ACC, int RM>
 __global__ void __launch_bounds__(kStageSide *kStageSide)
     contract_staged_kernel(const ContractArgs g) {
@@ -370,14 +380,23 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
     const bool live = i < g.rows && o < g.cols;
     const double *At = g.A + t * g.a_batch, *Bt = g.B + t * g.b_batch;
     int64_t k0 = -kStageK;
+    // Consecutive threads walk whichever axis of an operand has unit stride
+    // (k for a row-major operand, rows for one read down its columns, as
+    // AttnPass's dv reads the probabilities), so each warp's loads coalesce.
+    const bool a_kfast = g.a_k == 1 || g.a_row != 1, b_kfast = g.b_k == 1 || g.b_col != 1;
     auto stage = [&](int64_t base) {
         __syncthreads();
         for (int e = threadIdx.x; e < kStageSide * kStageK; e += kStageSide * kStageSide) {
-            const int r = e / kStageK, c = e % kStageK;
-            const int64_t k = base + c;
-            const bool kin = k < g.depth;
-            sA[r][c] = (kin && i0 + r < g.rows) ? __ldg(At + (i0 + r) * g.a_row + k * g.a_k) : 0.0;
-            sB[r][c] = (kin && o0 + r < g.cols) ? __ldg(Bt + (o0 + r) * g.b_col + k * g.b_k) : 0.0;
+            int r = a_kfast ? e / kStageK : e % kStageSide;
+            int c = a_kfast ? e % kStageK : e / kStageSide;
+            int64_t k = base + c;
+            sA[r][c] = (k < g.depth && i0 + r < g.rows) ? __ldg(At + (i0 + r) * g.a_row + k * g.a_k)
+                                                        : 0.0;
+            r = b_kfast ? e / kStageK : e % kStageSide;
+            c = b_kfast ? e % kStageK : e / kStageSide;
+            k = base + c;
+            sB[r][c] = (k < g.depth && o0 + r < g.cols) ? __ldg(Bt + (o0 + r) * g.b_col + k * g.b_k)
+                                                        : 0.0;
         }
         __syncthreads();
         k0 = base;
@@ -388,24 +407,35 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
         return ACC == DRIFT_ACC_FP64 ? t : rnd(t);
     };
     double v;
-    if (g.order == DRIFT_SEQUENTIAL || g.order == DRIFT_REVERSED ||
-        (g.order == DRIFT_BLOCKED && g.acc_block % kStageK == 0)) {
+    if (staged_walk(g.order, g.acc_block, g.window)) {
         // One staged chunk at a time with a fixed 32-term body: the chunk
         // walk of Dot.forward / backward, and of Dot.blocked when its chunks
         // end on chunk edges. (The per-term window check of the general walk
         // below cost 34 instructions per multiply-accumulate, against about 10
-        // here.)
+        // here.) Chunks sit at absolute multiples of 32 and cover the union of
+        // the tile's windows; each thread takes the part inside its own window
+        // (AttnPass's PREFIX and SUFFIX rows differ by at most 16 terms within
+        // a tile), the fixed body where that is the whole chunk.
         const bool rev = g.order == DRIFT_REVERSED, blk = g.order == DRIFT_BLOCKED;
-        const int64_t nch = (g.depth + kStageK - 1) / kStageK;
-        const int64_t fold_every = blk ? g.acc_block / kStageK : 0;
+        int64_t lo, n;
+        window_of(g, i, lo, n);  // rows past the end are clamped into range
+        lo = lo < g.depth ? lo : g.depth;
+        const int64_t hi = lo + (n < 0 ? 0 : (n < g.depth - lo ? n : g.depth - lo));
+        const int64_t last = (i0 + kStageSide < g.rows ? i0 + kStageSide : g.rows) - 1;
+        int64_t u_lo = 0, u_hi = g.depth;  // the tile's union of windows
+        if (g.window == DRIFT_WINDOW_PREFIX) u_hi = last + 1 < g.depth ? last + 1 : g.depth;
+        if (g.window == DRIFT_WINDOW_SUFFIX) u_lo = i0 < g.depth ? i0 : g.depth;
+        const int64_t ch_lo = u_lo / kStageK, ch_hi = (u_hi + kStageK - 1) / kStageK;
         double acc = 0.0, total = 0.0;
-        for (int64_t c = 0; c < nch; c++) {
-            const int64_t cc = rev ? nch - 1 - c : c;
-            stage(cc * kStageK);
+        for (int64_t c = 0; c < ch_hi - ch_lo; c++) {
+            const int64_t cc = rev ? ch_hi - 1 - c : ch_lo + c;
+            const int64_t c0 = cc * kStageK;
+            stage(c0);
             const double *ra = sA[ty], *rb = sB[tx];
-            const int64_t rest = g.depth - cc * kStageK;
-            const int len = rest < kStageK ? (int)rest : kStageK;
-            if (len == kStageK) {
+            const int qa = (int)(lo > c0 ? (lo - c0 < kStageK ? lo - c0 : kStageK) : 0);
+            const int qb = (int)(hi > c0 ? (hi - c0 < kStageK ? hi - c0 : kStageK) : 0);
+            if (qb <= qa) continue;  // nothing of this thread's window here
+            if (qa == 0 && qb == kStageK) {
                 // Eight steps at a time on the fast rounding with one range
                 // check for the eight; a miss redoes them exactly from the
                 // sum before them (as the tiled kernel's groups do across
@@ -438,11 +468,13 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
                     }
                 }
             } else if (!rev) {
-                for (int q = 0; q < len; q++) acc = step(acc, ra[q], rb[q]);
+                for (int q = qa; q < qb; q++) acc = step(acc, ra[q], rb[q]);
             } else {
-                for (int q = len - 1; q >= 0; q--) acc = step(acc, ra[q], rb[q]);
+                for (int q = qb - 1; q >= qa; q--) acc = step(acc, ra[q], rb[q]);
             }
-            if (blk && ((c + 1) % fold_every == 0 || c == nch - 1)) {  // Dot.blocked (:115-118)
+            // Dot.blocked (:115-118): a chunk of acc_block from the window's
+            // start (0 here) closes on a block edge or at the window's end.
+            if (blk && (((cc + 1) * kStageK) % g.acc_block == 0 || hi <= c0 + kStageK)) {
                 total = ACC == DRIFT_ACC_FP64
                             ? __dadd_rn(total, acc)
                             : (double)__double2float_rn(__dadd_rn(total, acc));
@@ -451,6 +483,7 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
         }
         v = blk ? total : acc;
     } else {
+        // FULL windows only (the launcher sends no other window here).
         auto term = [&](int64_t k) {
             if (k < k0 || k >= k0 + kStageK) stage(k - k % kStageK);  // the same k in every thread
             return __dmul_rn(sA[ty][k - k0], sB[tx][k - k0]);
@@ -668,6 +701,11 @@ static bool tiled_route(const ContractDesc &d) {
            op.b_k >= 0 && op.c_batch >= 0;
 }
 
+static bool staged_fits(const drift_contraction &op) {
+    return op.batch <= 65535 && (op.rows + kStageSide - 1) / kStageSide <= 65535 &&
+           (op.cols + kStageSide - 1) / kStageSide <= 0x7fffffffLL;
+}
+
 int64_t staged_tile_limit(const drift_policy *p) {
     // Measured on one B200 (tiled time / staged time, K = 512-2048): at 32
     // tiles of 64 x 64 the staged kernel won everywhere (FP64 1.29, pairwise
@@ -684,9 +722,9 @@ int64_t staged_tile_limit(const drift_policy *p) {
 int launch_contract_staged(const drift_policy *p, const ContractDesc &d, const int *skip,
                            int *route, cudaStream_t st) {
     const drift_contraction &op = d.op;
-    if (op.window != DRIFT_WINDOW_FULL || stochastic(p) || op.batch > 65535 ||
-        (op.rows + kStageSide - 1) / kStageSide > 65535 ||
-        (op.cols + kStageSide - 1) / kStageSide > 0x7fffffffLL)
+    const int64_t blk = std::max<int64_t>(1, p->acc_block);
+    if ((op.window != DRIFT_WINDOW_FULL && !staged_walk(p->order, blk, op.window)) ||
+        stochastic(p) || !staged_fits(op))
         return DRIFT_EINVAL;
     if (op.batch * op.rows * op.cols == 0) return DRIFT_OK;
     ContractArgs g = args_of(p, d);
@@ -735,6 +773,12 @@ int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
         if (op.causal || op.alpha != 1.0) contract_epilogue_kernel<<<grid, 128, 0, st>>>(g);
         return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
     }
+    // Ragged windows (and FULL ones the tiles do not take) in the orders the
+    // staged kernel walks chunk by chunk: one output per thread with the
+    // operands staged per 16 x 16 tile. Pairwise (a tree per row) and blocked
+    // chunks off the chunk edges stay on the per-thread kernel below.
+    if (!stochastic(p) && staged_walk(p->order, g.acc_block, d.op.window) && staged_fits(d.op))
+        return launch_contract_staged(p, d, nullptr, nullptr, st);
     if (!stochastic(p)) {
         const bool tr = p->acc_rounding == DRIFT_TRUNCATE;
         switch (p->acc) {

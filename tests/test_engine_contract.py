@@ -66,13 +66,14 @@ def test_attention_loops(d, acc, order, rm):
             assert s1 == s2
 
 
-@pytest.mark.parametrize("order", [0, 2, 3])
-@pytest.mark.parametrize("acc", [1, 2, 3])
-def test_long_ragged_windows(d, acc, order):
-    """Windows up to 150 terms: deep, uneven pairwise trees per row."""
-    rs = np.random.default_rng(acc + 7 * order)
-    p = (d.NumericPolicy.builder("c").acc(d.Acc(acc)).order(d.Order(order)).acc_block(32)
-         .build())
+@pytest.mark.parametrize("order,blk", [(0, 32), (1, 32), (2, 32), (3, 32), (3, 48), (3, 64)])
+@pytest.mark.parametrize("acc,rm", [(0, 0), (1, 0), (2, 0), (3, 0), (2, 2), (3, 2)])
+def test_long_ragged_windows(d, acc, rm, order, blk):
+    """Windows up to 150 terms: deep, uneven pairwise trees per row, and the
+    staged chunk walk's windows that start and end inside 32-term chunks."""
+    rs = np.random.default_rng(acc + 7 * order + 13 * rm + blk)
+    p = (d.NumericPolicy.builder("c").acc(d.Acc(acc)).order(d.Order(order)).acc_block(blk)
+         .acc_rounding(d.Rounding(rm)).build())
     for name, op, na, nb, nc in attention_ops(d, 2, 150, 4, 0.5):
         if name in ("context", "dv"):
             got, want, _, _ = run(d, p, op, heavy_tailed(rs, na), heavy_tailed(rs, nb),
