@@ -34,6 +34,7 @@
 // data. Nothing spins: each pass is a separate launch and the host reads a
 // flag between them.
 #include <algorithm>
+#include <type_traits>
 
 #include "codec.cuh"
 #include "internal.h"
@@ -366,13 +367,16 @@ __host__ __device__ inline bool staged_walk(int order, int64_t acc_block, int wi
 // 32 SMs each ran sixteen 2048-long chains per thread while the rest idled),
 // and the ragged PREFIX / SUFFIX windows of the attention matmuls in the
 // orders it walks chunk by chunk (staged_walk).
+// Four CTAs per SM (64 registers a thread): a batch-64 linear layer's 512
+// CTAs then fit the GPU in one wave.
 template <int ACC, int RM>
-__global__ void __launch_bounds__(kStageSide *kStageSide)
+__global__ void __launch_bounds__(kStageSide *kStageSide, 4)
     contract_staged_kernel(const ContractArgs g) {
     if (g.skip && *g.skip) return;  // the FP32 pipe (gemm32.cu) took the call
     if (g.route && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0)
         *g.route = DRIFT_ROUTE_STAGED;
-    __shared__ double sA[kStageSide][kStageK + 1], sB[kStageSide][kStageK + 1];
+    // Two buffers: the chunk walk fills one while it reads the other.
+    __shared__ double sA[2][kStageSide][kStageK + 1], sB[2][kStageSide][kStageK + 1];
     const int tx = threadIdx.x % kStageSide, ty = threadIdx.x / kStageSide;
     const int64_t t = blockIdx.z;
     const int64_t i0 = (int64_t)blockIdx.y * kStageSide, o0 = (int64_t)blockIdx.x * kStageSide;
@@ -384,20 +388,38 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
     // (k for a row-major operand, rows for one read down its columns, as
     // AttnPass's dv reads the probabilities), so each warp's loads coalesce.
     const bool a_kfast = g.a_k == 1 || g.a_row != 1, b_kfast = g.b_k == 1 || g.b_col != 1;
-    auto stage = [&](int64_t base) {
-        __syncthreads();
-        for (int e = threadIdx.x; e < kStageSide * kStageK; e += kStageSide * kStageSide) {
+    constexpr int kPer = kStageSide * kStageK / (kStageSide * kStageSide);  // elements per thread
+    double fa[kPer], fb[kPer];
+    auto fetch = [&](int64_t base) {  // this thread's share of a chunk, into registers
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            const int e = threadIdx.x + j * kStageSide * kStageSide;
             int r = a_kfast ? e / kStageK : e % kStageSide;
             int c = a_kfast ? e % kStageK : e / kStageSide;
             int64_t k = base + c;
-            sA[r][c] = (k < g.depth && i0 + r < g.rows) ? __ldg(At + (i0 + r) * g.a_row + k * g.a_k)
-                                                        : 0.0;
+            fa[j] = (k < g.depth && i0 + r < g.rows) ? __ldg(At + (i0 + r) * g.a_row + k * g.a_k)
+                                                     : 0.0;
             r = b_kfast ? e / kStageK : e % kStageSide;
             c = b_kfast ? e % kStageK : e / kStageSide;
             k = base + c;
-            sB[r][c] = (k < g.depth && o0 + r < g.cols) ? __ldg(Bt + (o0 + r) * g.b_col + k * g.b_k)
-                                                        : 0.0;
+            fb[j] = (k < g.depth && o0 + r < g.cols) ? __ldg(Bt + (o0 + r) * g.b_col + k * g.b_k)
+                                                     : 0.0;
         }
+    };
+    auto put = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < kPer; j++) {
+            const int e = threadIdx.x + j * kStageSide * kStageSide;
+            sA[buf][a_kfast ? e / kStageK : e % kStageSide][a_kfast ? e % kStageK : e / kStageSide] =
+                fa[j];
+            sB[buf][b_kfast ? e / kStageK : e % kStageSide][b_kfast ? e % kStageK : e / kStageSide] =
+                fb[j];
+        }
+    };
+    auto stage = [&](int64_t base) {  // the general walk: one buffer, staged on demand
+        __syncthreads();
+        fetch(base);
+        put(0);
         __syncthreads();
         k0 = base;
     };
@@ -411,11 +433,12 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
         // One staged chunk at a time with a fixed 32-term body: the chunk
         // walk of Dot.forward / backward, and of Dot.blocked when its chunks
         // end on chunk edges. (The per-term window check of the general walk
-        // below cost 34 instructions per multiply-accumulate, against about 10
-        // here.) Chunks sit at absolute multiples of 32 and cover the union of
-        // the tile's windows; each thread takes the part inside its own window
-        // (AttnPass's PREFIX and SUFFIX rows differ by at most 16 terms within
-        // a tile), the fixed body where that is the whole chunk.
+        // below cost 34 instructions per multiply-accumulate.) Chunks sit at
+        // absolute multiples of 32 and cover the union of the tile's windows;
+        // each thread takes the part inside its own window (AttnPass's PREFIX
+        // and SUFFIX rows differ by at most 16 terms within a tile), the fixed
+        // body where that is the whole chunk. The next chunk's loads are in
+        // flight while this one is summed.
         const bool rev = g.order == DRIFT_REVERSED, blk = g.order == DRIFT_BLOCKED;
         int64_t lo, n;
         window_of(g, i, lo, n);  // rows past the end are clamped into range
@@ -426,59 +449,88 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
         if (g.window == DRIFT_WINDOW_PREFIX) u_hi = last + 1 < g.depth ? last + 1 : g.depth;
         if (g.window == DRIFT_WINDOW_SUFFIX) u_lo = i0 < g.depth ? i0 : g.depth;
         const int64_t ch_lo = u_lo / kStageK, ch_hi = (u_hi + kStageK - 1) / kStageK;
+        const int64_t nc = ch_hi - ch_lo;
+        auto chunk_of = [&](int64_t c) { return rev ? ch_hi - 1 - c : ch_lo + c; };
         double acc = 0.0, total = 0.0;
-        for (int64_t c = 0; c < ch_hi - ch_lo; c++) {
-            const int64_t cc = rev ? ch_hi - 1 - c : ch_lo + c;
-            const int64_t c0 = cc * kStageK;
-            stage(c0);
-            const double *ra = sA[ty], *rb = sB[tx];
-            const int qa = (int)(lo > c0 ? (lo - c0 < kStageK ? lo - c0 : kStageK) : 0);
-            const int qb = (int)(hi > c0 ? (hi - c0 < kStageK ? hi - c0 : kStageK) : 0);
-            if (qb <= qa) continue;  // nothing of this thread's window here
-            if (qa == 0 && qb == kStageK) {
-                // Eight steps at a time on the fast rounding with one range
-                // check for the eight; a miss redoes them exactly from the
-                // sum before them (as the tiled kernel's groups do across
-                // outputs): every fast result that passes is the exact one.
-#pragma unroll 1
-                for (int q0 = 0; q0 < kStageK; q0 += 8) {
-                    double pr[8];
+        // A whole chunk, eight steps at a time on the fast rounding with one
+        // range check for the eight; a miss redoes them exactly from the sum
+        // before them (as the tiled kernel's groups do across outputs): every
+        // fast result that passes is the exact one. REV walks it downwards.
+        auto whole = [&](const double *ra, const double *rb, auto rev_c) {
+            constexpr bool REV = decltype(rev_c)::value;
+#pragma unroll 2
+            for (int q0 = 0; q0 < kStageK; q0 += 8) {
+                const double *pa = REV ? ra + (kStageK - 1 - q0) : ra + q0;
+                const double *pb = REV ? rb + (kStageK - 1 - q0) : rb + q0;
+                double pr[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) pr[j] = __dmul_rn(pa[REV ? -j : j], pb[REV ? -j : j]);
+                if constexpr (ACC == DRIFT_ACC_FP64) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) acc = __dadd_rn(acc, pr[j]);
+                } else {
+                    using R = AccRound<ACC, RM>;
+                    const double s0 = acc;
+                    bool ok = true;
 #pragma unroll
                     for (int j = 0; j < 8; j++) {
-                        const int q = rev ? kStageK - 1 - (q0 + j) : q0 + j;
-                        pr[j] = __dmul_rn(ra[q], rb[q]);
+                        acc = R::fast(__dadd_rn(acc, pr[j]));
+                        ok = ok & R::ok(acc);
                     }
-                    if constexpr (ACC == DRIFT_ACC_FP64) {
+                    if (!ok) {
+                        acc = s0;
 #pragma unroll
-                        for (int j = 0; j < 8; j++) acc = __dadd_rn(acc, pr[j]);
-                    } else {
-                        using R = AccRound<ACC, RM>;
-                        const double s0 = acc;
-                        bool ok = true;
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            acc = R::fast(__dadd_rn(acc, pr[j]));
-                            ok = ok & R::ok(acc);
-                        }
-                        if (!ok) {
-                            acc = s0;
-#pragma unroll
-                            for (int j = 0; j < 8; j++) acc = R::exact(__dadd_rn(acc, pr[j]));
-                        }
+                        for (int j = 0; j < 8; j++) acc = R::exact(__dadd_rn(acc, pr[j]));
                     }
                 }
-            } else if (!rev) {
-                for (int q = qa; q < qb; q++) acc = step(acc, ra[q], rb[q]);
-            } else {
-                for (int q = qb - 1; q >= qa; q--) acc = step(acc, ra[q], rb[q]);
             }
-            // Dot.blocked (:115-118): a chunk of acc_block from the window's
-            // start (0 here) closes on a block edge or at the window's end.
-            if (blk && (((cc + 1) * kStageK) % g.acc_block == 0 || hi <= c0 + kStageK)) {
-                total = ACC == DRIFT_ACC_FP64
-                            ? __dadd_rn(total, acc)
-                            : (double)__double2float_rn(__dadd_rn(total, acc));
-                acc = 0.0;
+        };
+        // FP64 chains (a bare add per step) fetch the next chunk while they
+        // sum this one. The rounding chains fetch at the top of each chunk:
+        // holding the next chunk in registers cost them more than the hidden
+        // load latency gave back (measured on one B200). Either way a buffer
+        // is written only after every thread has passed the barrier that
+        // follows its last reading, so one barrier per chunk suffices.
+        constexpr bool PF = ACC == DRIFT_ACC_FP64;
+        if (PF && nc > 0) {
+            fetch(chunk_of(0) * kStageK);
+            put(0);
+        }
+        __syncthreads();
+        for (int64_t c = 0; c < nc; c++) {
+            const int64_t cc = chunk_of(c), c0 = cc * kStageK;
+            if (!PF) {
+                fetch(c0);
+                put(c & 1);  // last read two chunks ago
+                __syncthreads();
+            } else if (c + 1 < nc) {
+                fetch(chunk_of(c + 1) * kStageK);  // in flight during the sums
+            }
+            const double *ra = sA[c & 1][ty], *rb = sB[c & 1][tx];
+            const int qa = (int)(lo > c0 ? (lo - c0 < kStageK ? lo - c0 : kStageK) : 0);
+            const int qb = (int)(hi > c0 ? (hi - c0 < kStageK ? hi - c0 : kStageK) : 0);
+            if (qa < qb) {
+                if (qa == 0 && qb == kStageK) {
+                    if (rev) whole(ra, rb, std::true_type{});
+                    else whole(ra, rb, std::false_type{});
+                } else if (!rev) {
+                    for (int q = qa; q < qb; q++) acc = step(acc, ra[q], rb[q]);
+                } else {
+                    for (int q = qb - 1; q >= qa; q--) acc = step(acc, ra[q], rb[q]);
+                }
+                // Dot.blocked (:115-118): a chunk of acc_block from the
+                // window's start (0 here) closes on a block edge or at the
+                // window's end.
+                if (blk && (((cc + 1) * kStageK) % g.acc_block == 0 || hi <= c0 + kStageK)) {
+                    total = ACC == DRIFT_ACC_FP64
+                                ? __dadd_rn(total, acc)
+                                : (double)__double2float_rn(__dadd_rn(total, acc));
+                    acc = 0.0;
+                }
+            }
+            if (PF) {
+                if (c + 1 < nc) put((c + 1) & 1);  // that buffer was last read before the barrier
+                __syncthreads();
             }
         }
         v = blk ? total : acc;
@@ -486,7 +538,7 @@ __global__ void __launch_bounds__(kStageSide *kStageSide)
         // FULL windows only (the launcher sends no other window here).
         auto term = [&](int64_t k) {
             if (k < k0 || k >= k0 + kStageK) stage(k - k % kStageK);  // the same k in every thread
-            return __dmul_rn(sA[ty][k - k0], sB[tx][k - k0]);
+            return __dmul_rn(sA[0][ty][k - k0], sB[0][tx][k - k0]);
         };
         v = dot_terms<ACC>(g, term, g.depth, rnd);
     }
