@@ -375,8 +375,11 @@ __global__ void __launch_bounds__(kStageSide *kStageSide, 4)
     if (g.skip && *g.skip) return;  // the FP32 pipe (gemm32.cu) took the call
     if (g.route && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 0)
         *g.route = DRIFT_ROUTE_STAGED;
-    // Two buffers: the chunk walk fills one while it reads the other.
-    __shared__ double sA[2][kStageSide][kStageK + 1], sB[2][kStageSide][kStageK + 1];
+    // Two buffers: the chunk walk fills one while it reads the other. Rows are
+    // padded to an even length so each starts 16-byte aligned and the fixed
+    // body reads two terms per load.
+    constexpr int kRow = kStageK + 2;
+    __shared__ __align__(16) double sA[2][kStageSide][kRow], sB[2][kStageSide][kRow];
     const int tx = threadIdx.x % kStageSide, ty = threadIdx.x / kStageSide;
     const int64_t t = blockIdx.z;
     const int64_t i0 = (int64_t)blockIdx.y * kStageSide, o0 = (int64_t)blockIdx.x * kStageSide;
@@ -460,11 +463,19 @@ __global__ void __launch_bounds__(kStageSide *kStageSide, 4)
             constexpr bool REV = decltype(rev_c)::value;
 #pragma unroll 2
             for (int q0 = 0; q0 < kStageK; q0 += 8) {
-                const double *pa = REV ? ra + (kStageK - 1 - q0) : ra + q0;
-                const double *pb = REV ? rb + (kStageK - 1 - q0) : rb + q0;
+                // Terms q0 .. q0+7 of the walk, read as four aligned pairs
+                // (reversed: pairs from the top of the chunk down).
+                const double *pa = REV ? ra + (kStageK - 2 - q0) : ra + q0;
+                const double *pb = REV ? rb + (kStageK - 2 - q0) : rb + q0;
                 double pr[8];
 #pragma unroll
-                for (int j = 0; j < 8; j++) pr[j] = __dmul_rn(pa[REV ? -j : j], pb[REV ? -j : j]);
+                for (int jj = 0; jj < 4; jj++) {
+                    const int off = REV ? -2 * jj : 2 * jj;
+                    const double2 xa = *reinterpret_cast<const double2 *>(pa + off);
+                    const double2 xb = *reinterpret_cast<const double2 *>(pb + off);
+                    pr[2 * jj] = __dmul_rn(REV ? xa.y : xa.x, REV ? xb.y : xb.x);
+                    pr[2 * jj + 1] = __dmul_rn(REV ? xa.x : xa.y, REV ? xb.x : xb.y);
+                }
                 if constexpr (ACC == DRIFT_ACC_FP64) {
 #pragma unroll
                     for (int j = 0; j < 8; j++) acc = __dadd_rn(acc, pr[j]);
