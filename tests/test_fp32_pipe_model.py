@@ -109,7 +109,7 @@ def operands(case, rs):
 @pytest.mark.parametrize("case", ["bf16", "e4m3", "e2m1", "e5m2", "subnormal", "overflow"])
 @pytest.mark.parametrize("order,blk", [(0, 32), (1, 32), (3, 32), (3, 48)])
 def test_fp32_chain_matches_double_then_float(case, order, blk):
-    rs = np.random.default_rng(hash(case) % 1000 + order + blk)
+    rs = np.random.default_rng(sum(map(ord, case)) + 10 * order + blk)
     A, B = operands(case, rs)
     assert admitted(A, B)
     want, _ = O.gemm(O.policy(acc=1, order=order, acc_block=blk), M, N, K, A, 0, K, 1, B, 0, K, 1,
