@@ -940,7 +940,7 @@ int drift_quantize_dev_noalloc(const drift_policy *p, int fmt, int rounding, con
                                            d_rng_state, (unsigned long long *)d_clamped, d_err,
                                            (cudaStream_t)stream);
     if (rc == DRIFT_ENOMEM)
-        return fail(rc, "too many items for the fixed scratch array (DRIFT_NOALLOC_MAX_ITEMS)");
+        return fail(rc, "a stochastic cast of more items than the fixed scratch array holds (DRIFT_NOALLOC_MAX_ITEMS)");
     return rc ? fail(rc, "no-allocation quantize launch") : DRIFT_OK;
 }
 

@@ -608,31 +608,27 @@ int launch_quantize_noalloc(const drift_policy *p, int fmt, int rm, const double
         return DRIFT_OK;
     }
     QuantOp op;
-    if (!fmt_desc(fmt, &op.f)) return DRIFT_EINVAL;
-    if (rm < 0 || rm > 2) return DRIFT_EINVAL;
-    if (p->scaling < 0 || p->scaling > 2) return DRIFT_EINVAL;
-    if (p->scaling == DRIFT_MX_BLOCK && p->scale_block <= 0) return DRIFT_EINVAL;
-    const int64_t item_len = p->scaling == DRIFT_MX_BLOCK ? p->scale_block : 32;
+    int64_t item_len = 0;
+    int rc = make_quant_op(p, fmt, rm, d_src, d_dst, d_scale, scale, &op, &item_len);
+    if (rc) return rc;
+    // The array's address is looked up on the first call that casts, whatever
+    // its rounding or size, so that a first call made before a stream capture
+    // leaves nothing to look up inside it.
+    char *base = nullptr;
+    rc = noalloc_scratch(&base);
+    if (rc) return rc;
     const int64_t items = (n + item_len - 1) / item_len;
-    if (items > DRIFT_NOALLOC_MAX_ITEMS) return DRIFT_ENOMEM;
-    if (n == 0) return DRIFT_OK;
-    op.src = d_src;
-    op.dst = d_dst;
-    op.rm = rm;
-    op.scaling = p->scaling;
-    op.headroom = p->mx_headroom;
-    op.d_scale = p->scaling == DRIFT_PER_TENSOR ? d_scale : nullptr;
-    op.scale = scale;
-    op.inv = 1.0 / scale;
     const int64_t grid = (items + kItemsPerCta - 1) / kItemsPerCta;
+    if (grid > 0x7fffffffLL) return DRIFT_EINVAL;
+    // Only stochastic rounding uses the array; the other casts take one pass
+    // and have no size limit beyond the launch's.
+    if (rm == DRIFT_STOCHASTIC && items > DRIFT_NOALLOC_MAX_ITEMS) return DRIFT_ENOMEM;
+    if (n == 0) return DRIFT_OK;
     SrArgs sr{nullptr, nullptr, nullptr, d_clamped, d_err};
     if (rm != DRIFT_STOCHASTIC) {
         elem_kernel<QuantOp, 0><<<(unsigned)grid, kThreads, 0, st>>>(op, n, item_len, sr);
         return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
     }
-    char *base = nullptr;
-    const int rc = noalloc_scratch(&base);
-    if (rc) return rc;
     sr.cta_counts = (uint64_t *)base;
     uint64_t *state_before = (uint64_t *)(base + (size_t)kNoAllocCtas * sizeof(uint64_t));
     sr.item_counts = (uint32_t *)(base + (size_t)kNoAllocCtas * sizeof(uint64_t) + 256);

@@ -276,18 +276,26 @@ DRIFT_API int drift_per_tensor_scale_dev(drift_ctx *ctx, int fmt,
  * The cast is the same as drift_quantize_dev's, bit for bit. Stochastic
  * rounding needs scratch space; it comes from one array of about 1 MiB that
  * the library declares statically, which every GPU that loads the library
- * holds until the process exits. That bounds one call to
+ * holds until the process exits. That bounds one stochastic call to
  * DRIFT_NOALLOC_MAX_ITEMS items (groups of 32 elements, or MX blocks of
  * scale_block elements): n up to 8,388,608 elements for an element-wise cast
- * with 32-element items. Larger calls return DRIFT_ENOMEM and do nothing.
+ * with 32-element items. Larger stochastic calls return DRIFT_ENOMEM and do
+ * nothing. Nearest-even and truncating casts use no scratch and have no such
+ * limit.
  *
- * The first call on each device looks up the array's device address with
- * that device current; make that first call before any stream capture. All
- * calls share the array, so calls that overlap on the GPU (other streams, or
- * other threads on the same device) race and must be serialised by the
- * caller. Device-side errors (NaN into a format without NaN, a needed draw
- * with d_rng_state NULL) are ORed into the caller's device int *d_err, which
- * the caller clears and reads. Nothing is allocated or freed by the call.
+ * The first call on each device that casts (any format but none, any
+ * rounding, any n) looks up the array's device address with that device
+ * current; make that first call before any stream capture. CUDA loads the
+ * library's device code and this array onto a device lazily, when the
+ * library first launches work there, unless the process runs with
+ * CUDA_MODULE_LOADING=EAGER; a caller whose budget must also cover that load
+ * makes one small call (for example a stochastic cast of 32 elements) on
+ * each device before its budgeted region. All calls share the array, so
+ * calls that overlap on the GPU (other streams, or other threads on the same
+ * device) race and must be serialised by the caller. Device-side errors (NaN
+ * into a format without NaN, a needed draw with d_rng_state NULL) are ORed
+ * into the caller's device int *d_err, which the caller clears and reads.
+ * Nothing is allocated or freed by the call.
  */
 #define DRIFT_NOALLOC_MAX_ITEMS (1 << 18)
 DRIFT_API int drift_quantize_dev_noalloc(const drift_policy *p, int fmt,
