@@ -51,19 +51,10 @@ SWEEP_NAMES = ["fp32 sequential", "fp32 pairwise", "fp32 blocked", "fp16 sequent
 
 
 def sweep_policies(d):
-    """RealDotSweep's policy list (RealDotSweep.java:212-223): the 9
-    accumulator x order policies, the bf16 cast, e4m3 per-tensor and e4m3 MX32."""
-    F, A, O, S = d.Formats, d.Acc, d.Order, d.Scaling
-    b = d.NumericPolicy.builder
-    ps = []
-    for acc in (A.FP32, A.FP16, A.BF16):
-        for o in (O.SEQUENTIAL, O.PAIRWISE, O.BLOCKED):
-            name = f"{acc.name.lower()} {o.name.lower()}"
-            ps.append(b(name).acc(acc).order(o).acc_block(32).build())
-    ps.append(b("bf16 cast").input(F.BF16).build())
-    ps.append(b("e4m3 per-tensor cast").input(F.E4M3).scaling(S.PER_TENSOR).build())
-    ps.append(b("e4m3 mx32 cast").input(F.E4M3).scaling(S.MX_BLOCK).build())
-    return ps
+    """RealDotSweep's policy list (RealDotSweep.java:212-223)."""
+    from drift_b200 import sweeps
+
+    return sweeps.policy_sweep_policies()
 
 
 # ------------------------------------------------------------------ clocks
@@ -127,59 +118,77 @@ def dist_setup():
 
 # ------------------------------------------------------------------ CPU baseline
 
-def cpu_baseline(size: int, budget_s: float, threads: int | None = None):
-    """Times the oracle (the C restatement of the Java path) on this host's
-    cores over a bounded sample of the same sweep: for each of the 13 GEMMs,
-    R rows of A against C rows of B with the full K = size terms (R x C
-    outputs). Per-tensor scales come from the full tensors, as in the real
-    job; the casts themselves run before the clock starts (over the whole job
-    they are about 1e-4 of the contraction work). Returns (MAC/s, threads,
-    description)."""
-    import numpy as np
-    from oracle import oracle as O
+# The fixed CPU sample, the same in the engine arm's cpu_baseline leg and in
+# the reference arm: for each of the 13 GEMMs, SAMPLE_ROWS rows of A against
+# SAMPLE_COLS rows of B with the full K terms.
+SAMPLE_ROWS, SAMPLE_COLS = 64, 512
 
-    threads = threads or os.cpu_count() or 1
-    rs = np.random.default_rng(0)
-    K = size
-    cols = min(size, 512)
-    full_a = rs.standard_normal(size * K) * np.exp(rs.standard_normal(size * K))
-    full_b = rs.standard_normal(size * K) * np.exp(rs.standard_normal(size * K))
-    amax_a, amax_b = O.amax(full_a), O.amax(full_b)
-    pols = [O.policy(acc=O.ACC_FP64)]
-    for acc in (O.ACC_FP32, O.ACC_FP16, O.ACC_BF16):
-        for order in (O.SEQUENTIAL, O.PAIRWISE, O.BLOCKED):
-            pols.append(O.policy(acc=acc, order=order))
-    pols.append(O.policy(input_format=O.BF16))
-    pols.append(O.policy(input_format=O.E4M3, scaling=O.PER_TENSOR))
-    pols.append(O.policy(input_format=O.E4M3, scaling=O.MX_BLOCK))
-    B = full_b[:cols * K].copy()
-    # Calibrate the row count so the timed sample takes about budget_s.
-    A1 = full_a[:K * threads].copy()
-    t0 = time.perf_counter()
-    O.gemm(pols[4], threads, min(cols, 64), K, A1, 0, K, 1, B, 0, K, 1, threads=threads)
-    per_mac = (time.perf_counter() - t0) / (threads * min(cols, 64) * K)
-    rows = int(budget_s / len(pols) / (per_mac * cols * K * 1.5)) // threads * threads
-    rows = max(threads, min(rows, size))
-    A = full_a[:rows * K].copy()
-    operands = []
-    for p in pols:
-        if p.input_format < 0:
-            operands.append((A, B))
-            continue
-        f = p.input_format
-        sa = O.per_tensor_scale(f, amax_a) if p.scaling == O.PER_TENSOR else 1.0
-        sb = O.per_tensor_scale(f, amax_b) if p.scaling == O.PER_TENSOR else 1.0
-        operands.append((O.quantize(p, f, 0, A, sa)[0], O.quantize(p, f, 0, B, sb)[0]))
-    macs = 0
-    t0 = time.perf_counter()
-    for p, (qa, qb) in zip(pols, operands):
-        O.gemm(p, rows, cols, K, qa, 0, K, 1, qb, 0, K, 1, threads=threads)
-        macs += rows * cols * K
-    dt = time.perf_counter() - t0
-    desc = (f"oracle (C restatement of the Java path, -O2, no FMA) on {threads} host threads: "
-            f"{len(pols)} GEMMs of {rows} x {cols} outputs with K={K}; {macs:.3e} MACs in "
-            f"{dt:.1f} s")
-    return macs / dt, threads, desc
+
+class CpuSample:
+    """The sweep's 13 GEMMs on the oracle (the C restatement of the Java
+    path) over one fixed row sample of the same workload: SAMPLE_ROWS x
+    SAMPLE_COLS outputs each, full K = size terms. Per-tensor scales come from
+    the full tensors, as in the real job; the casts run once, before any
+    timing (over the whole job they are about 1e-4 of the contraction work)."""
+
+    def __init__(self, size: int, threads: int | None = None):
+        import numpy as np
+        from oracle import oracle as O
+
+        self.O = O
+        self.threads = threads or os.cpu_count() or 1
+        self.K = K = size
+        self.rows = min(size, SAMPLE_ROWS)
+        self.cols = min(size, SAMPLE_COLS)
+        rs = np.random.default_rng(0)
+        full_a = rs.standard_normal(size * K) * np.exp(rs.standard_normal(size * K))
+        full_b = rs.standard_normal(size * K) * np.exp(rs.standard_normal(size * K))
+        amax_a, amax_b = O.amax(full_a), O.amax(full_b)
+        pols = [O.policy(acc=O.ACC_FP64)]
+        for acc in (O.ACC_FP32, O.ACC_FP16, O.ACC_BF16):
+            for order in (O.SEQUENTIAL, O.PAIRWISE, O.BLOCKED):
+                pols.append(O.policy(acc=acc, order=order))
+        pols.append(O.policy(input_format=O.BF16))
+        pols.append(O.policy(input_format=O.E4M3, scaling=O.PER_TENSOR))
+        pols.append(O.policy(input_format=O.E4M3, scaling=O.MX_BLOCK))
+        A = full_a[:self.rows * K].copy()
+        B = full_b[:self.cols * K].copy()
+        del full_a, full_b
+        self.work = []
+        for p in pols:
+            if p.input_format < 0:
+                self.work.append((p, A, B))
+                continue
+            f = p.input_format
+            sa = O.per_tensor_scale(f, amax_a) if p.scaling == O.PER_TENSOR else 1.0
+            sb = O.per_tensor_scale(f, amax_b) if p.scaling == O.PER_TENSOR else 1.0
+            self.work.append((p, O.quantize(p, f, 0, A, sa)[0], O.quantize(p, f, 0, B, sb)[0]))
+        self.macs = len(pols) * self.rows * self.cols * K
+
+    def run(self) -> float:
+        """One pass over the sample; returns its wall time in seconds."""
+        t0 = time.perf_counter()
+        for p, qa, qb in self.work:
+            self.O.gemm(p, self.rows, self.cols, self.K, qa, 0, self.K, 1, qb, 0, self.K, 1,
+                        threads=self.threads)
+        return time.perf_counter() - t0
+
+    def describe(self, seconds: float) -> str:
+        return (f"oracle (C restatement of the Java path, -O2, no FMA) on {self.threads} host "
+                f"threads: {len(self.work)} GEMMs of {self.rows} x {self.cols} outputs with "
+                f"K={self.K} (the first rows of A and B of the seed-0 workload); "
+                f"{self.macs:.3e} MACs in {seconds:.2f} s")
+
+
+def cpu_baseline(size: int, repeats: int = 3):
+    """The engine arm's cpu_baseline leg: the fixed sample, timed `repeats`
+    times after one untimed pass; the median pass. Returns (MAC/s, threads,
+    description)."""
+    smp = CpuSample(size)
+    smp.run()
+    times = sorted(smp.run() for _ in range(max(1, repeats)))
+    t = statistics.median(times)
+    return smp.macs / t, smp.threads, smp.describe(t)
 
 
 # ------------------------------------------------------------------ engine arm
@@ -207,15 +216,9 @@ def run_engine(args):
     dev = torch.device("cuda", local)
 
     def make_inputs(seed):
-        g = torch.Generator(device=dev)
-        g.manual_seed(1000 + seed)
-        # Full 53-bit doubles, as Java's nextGaussian gives (the reference's
-        # weights and embeddings start from it).
-        x = torch.randn(S, S, device=dev, generator=g, dtype=torch.float64)
-        x *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float64))
-        y = torch.randn(S, S, device=dev, generator=g, dtype=torch.float64)
-        y *= torch.exp(torch.randn(S, S, device=dev, generator=g, dtype=torch.float64))
-        return x, y
+        from drift_b200 import sweeps
+
+        return sweeps.policy_sweep_inputs(S, seed, dev)
 
     seed = ddist.seeds_for(rank, world, 0)[0]  # this rank's seed, the same every step
     A, B = make_inputs(seed)
@@ -311,6 +314,10 @@ def run_engine(args):
     ms_max = ddist.max_over_ranks(t_start.elapsed_time(t_end), pg, dev)
     macs_per_step_rank = (n_pol + 1) * M * N * K
     value = macs_per_step_rank * world * args.steps / (ms_max * 1e-3)
+    # The 12 policies alone: their MACs over the step time less the exact
+    # GEMM's device time (last step's events, max over ranks).
+    exact_ms = ddist.max_over_ranks(gemm_ms[0], pg, dev)
+    value_excl = n_pol * M * N * K * world / ((ms_max / args.steps - exact_ms) * 1e-3)
 
     # Roofline of the dominant kernel, the double-precision contraction
     # (gemm_kernel, every contraction not on the FP32 pipe): FP64-pipe work is
@@ -362,7 +369,7 @@ def run_engine(args):
 
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
-        v, cores, desc = cpu_baseline(S, args.cpu_budget)
+        v, cores, desc = cpu_baseline(S)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}
 
     ddist.finish(pg)
@@ -372,6 +379,9 @@ def run_engine(args):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+        "value_excluding_exact": value_excl,
+        "value_excluding_exact_note": "the 12 policies' MACs over the step time less the exact "
+                                      "FP64 GEMM's device time",
         "data": "synthetic: N(0,1) x lognormal(0,1) doubles (53-bit, like Java's nextGaussian), "
                 "seeded per rank",
         "config": {"workload": f"policy sweep GEMM M=N=K={S}, 12 policies + exact FP64, "
@@ -470,31 +480,32 @@ def run_reference(args):
     world, rank, _ = dist_setup()
     if rank != 0:
         return 0
-    vals = []
-    desc = cores = None
+    smp = CpuSample(args.size)
     for _ in range(args.warmup):
-        cpu_baseline(args.size, min(5.0, args.cpu_budget / 4))
-    for _ in range(args.steps):
-        v, cores, desc = cpu_baseline(args.size, args.cpu_budget / max(1, args.steps))
-        vals.append(v)
-    value = statistics.median(vals)
+        smp.run()
+    times = [smp.run() for _ in range(args.steps)]
+    t = statistics.median(times)
+    value = smp.macs / t
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup,
-        # A full step's 13 GEMMs at the sampled rate (each timed step is a bounded row sample).
-        "ms_per_step": 13 * float(args.size) ** 3 / value * 1e3, "higher_is_better": True,
+        # Each step is one pass over the fixed sample; this is its measured time.
+        "ms_per_step": t * 1e3, "higher_is_better": True,
+        "full_step_ms_extrapolated": 13 * float(args.size) ** 3 / value * 1e3,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "impl": "reference",
         "data": "synthetic: N(0,1) x lognormal(0,1) doubles (53-bit, like Java's nextGaussian)",
         "config": {"workload": f"policy sweep GEMM M=N=K={args.size}, 12 policies + exact FP64, "
                                f"1 seed per rank per step", "M": args.size, "N": args.size,
                    "K": args.size, "policies": SWEEP_NAMES,
                    "seeds_per_step": 1, "parallelism": "host threads of rank 0"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": desc},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": smp.threads, "kind": "port",
+                         "sample": smp.describe(t)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "no JVM on this image: the reference's Java path is timed through its C "
-                "restatement (the oracle), with all host threads, on a bounded row sample of "
-                "each step; ms_per_step is a full step at that rate",
+                "restatement (the oracle), with all host threads. A step is one pass over a "
+                "fixed row sample of the workload (the same sample as the engine arm's "
+                "cpu_baseline); ms_per_step is that pass's median time, and "
+                "full_step_ms_extrapolated is a whole step at the measured rate",
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -712,7 +723,6 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-budget", type=float, default=20.0, help="seconds of CPU baseline work")
     ap.add_argument("--mode", choices=["sweep", "kernels", "train", "configs"], default="sweep",
                     help="kernels: time each policy's contraction alone (for profiling)")
     ap.add_argument("--policies", default="", help="kernels mode: comma-separated policy names")

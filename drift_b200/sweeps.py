@@ -9,6 +9,8 @@ real_dot_batch  RealDotSweep (java/src/main/java/io/drift/tools/RealDotSweep.jav
 mx_gemm         The block-scaled GEMM study: e4m3 / e2m1 operands under per-tensor
                 and MX (spec and +1) scaling, FP32 sequential accumulation, with
                 clamps per vector pair and per block pair and the relative error.
+policy_sweep_*  The large policy sweep: square GEMMs under RealDotSweep's 12
+                accumulator x order x cast policies plus the FP64 exact GEMM.
 
 Inputs are synthetic (seeded): N(0,1) x lognormal(0, sigma) vectors, windows
 of an N(0,1) embedding table, and Kaiming-normal weights. Every cast and dot
@@ -306,3 +308,38 @@ def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0) -> 
                        "clamped_per_pair": per_pair,
                        "clamped_per_block_pair": per_pair / (size // 32)}
     return res
+
+
+# ------------------------------------------------------------------ policy sweep
+
+def policy_sweep_policies() -> List[NumericPolicy]:
+    """RealDotSweep's policy list (RealDotSweep.java:212-223): the 9
+    accumulator x order policies (blocked in chunks of 32), the bf16 cast,
+    e4m3 per-tensor and e4m3 MX32, each with its cast of both operands."""
+    b = NumericPolicy.builder
+    ps = []
+    for acc in (Acc.FP32, Acc.FP16, Acc.BF16):
+        for o in (Order.SEQUENTIAL, Order.PAIRWISE, Order.BLOCKED):
+            ps.append(b(f"{acc.name.lower()} {o.name.lower()}").acc(acc).order(o).acc_block(32).build())
+    ps.append(b("bf16 cast").input(Formats.BF16).build())
+    ps.append(b("e4m3 per-tensor cast").input(Formats.E4M3).scaling(Scaling.PER_TENSOR).build())
+    ps.append(b("e4m3 mx32 cast").input(Formats.E4M3).scaling(Scaling.MX_BLOCK).build())
+    return ps
+
+
+def policy_sweep_inputs(size: int, seed: int, device, rows: Optional[int] = None):
+    """The sweep's operands for one seed, generated on the device: A and B of
+    `rows` (default `size`) x `size` doubles, each element N(0,1) x
+    lognormal(0,1) with a full 53-bit significand, as Java's nextGaussian
+    gives (the reference's weights and embeddings start from it). Row r of a
+    larger draw equals row r of a smaller one only for the same `rows`."""
+    import torch
+
+    rows = size if rows is None else rows
+    g = torch.Generator(device=device)
+    g.manual_seed(1000 + seed)
+    x = torch.randn(rows, size, device=device, generator=g, dtype=torch.float64)
+    x *= torch.exp(torch.randn(rows, size, device=device, generator=g, dtype=torch.float64))
+    y = torch.randn(rows, size, device=device, generator=g, dtype=torch.float64)
+    y *= torch.exp(torch.randn(rows, size, device=device, generator=g, dtype=torch.float64))
+    return x, y
