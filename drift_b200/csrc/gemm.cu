@@ -7,9 +7,10 @@
 // exactly the Java order, and parallelism comes only from independent outputs.
 //
 // Per multiply-accumulate: one DMUL and one DADD (never fused: Java rounds the
-// product to double before the add, Dot.java:46/:54/:63) and, for narrow
-// accumulators, the fast rounding of codec.cuh, validated for eight of a
-// thread's sixteen outputs at a time.
+// product to double before the add, Dot.java:46/:54/:63) and, for the FP32,
+// FP16 and BF16 accumulators, the fast rounding of codec.cuh (FastForm: one
+// LOP3 and two DFMAs), its range words folded and checked once per group of
+// eight or sixteen of a thread's outputs.
 //
 // Tiling. A CTA of 256 threads owns a 64x64 output tile; thread (ty, tx) owns
 // rows ty + 16i and columns tx + 16j (i, j < 4), so the sixteen threads that
@@ -70,9 +71,11 @@ constexpr int kMaxPairwiseDepth = 30;  // stack depth; enough for any int32 K
 // the narrow accumulators' rounding makes a long tile body fall out of the
 // instruction cache, so they unroll less (pairwise least, as its per-tile
 // merge code is the largest); FP64/FP32 bodies are small and unroll fully.
+// (With FastForm's shorter step, FP16/BF16 sequential gained 3% going from
+// 2 to 4.)
 template <int ACC, int ORDER>
 constexpr int kp_unroll() {
-    return ORDER == DRIFT_PAIRWISE ? 1 : (ACC == DRIFT_ACC_FP64 || ACC == DRIFT_ACC_FP32) ? 8 : 2;
+    return ORDER == DRIFT_PAIRWISE ? 1 : (ACC == DRIFT_ACC_FP64 || ACC == DRIFT_ACC_FP32) ? 8 : 4;
 }
 
 enum SegMode { SEG_NONE = 0, SEG_TILE = 1, SEG_SCHED = 2 };
@@ -116,37 +119,11 @@ constexpr int mac_group() {
     return ORDER == DRIFT_SEQUENTIAL || ORDER == DRIFT_REVERSED ? TM : GROUP_ROWS;
 }
 
-// Rounds sixteen sums in place as the accumulator does (Dot.java:54, :63,
-// :99, :224). The rounded value overwrites the sum and the sum is kept aside
-// only until its group is validated, so no copy is needed on the fast path.
-template <int ACC, int RM>
-__device__ __forceinline__ void round16(double (&t)[TM][TN]) {
-    using R = AccRound<ACC, RM>;
-    if constexpr (ACC != DRIFT_ACC_FP64) {
-#pragma unroll
-        for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
-            double keep[GROUP_ROWS][TN];
-            bool ok = true;
-#pragma unroll
-            for (int i = 0; i < GROUP_ROWS; i++)
-#pragma unroll
-                for (int j = 0; j < TN; j++) {
-                    keep[i][j] = t[i0 + i][j];
-                    t[i0 + i][j] = R::fast(keep[i][j]);
-                    ok = ok & R::ok(t[i0 + i][j]);
-                }
-            if (!ok) {
-#pragma unroll
-                for (int i = 0; i < GROUP_ROWS; i++)
-#pragma unroll
-                    for (int j = 0; j < TN; j++) t[i0 + i][j] = R::exact(keep[i][j]);
-            }
-        }
-    }
-}
-
 // One k step for the thread's 16 outputs: acc = round(acc + a_i * b_j), the
-// rounded value written straight into the accumulator.
+// rounded value written straight into the accumulator. Each group of G rows
+// folds its sums' range words into one word, checked once: a miss (zero, the
+// accumulator's subnormal range, its top binade, Inf, NaN) recomputes that
+// group's sums exactly from the kept sums.
 // FIRST starts a fresh sum: acc = round(0.0 + a_i * b_j), whatever acc held
 // (0.0 + p is not p when p is -0.0, so the add stays).
 template <int ACC, int RM, int G = GROUP_ROWS, bool FIRST = false>
@@ -162,17 +139,21 @@ __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[T
     } else {
 #pragma unroll
         for (int i0 = 0; i0 < TM; i0 += G) {
-            double t[G][TN];
-            bool ok = true;
+            double t[G][TN];       // the sums, kept until the group is validated
+            unsigned run = 0, u[G][TN];
 #pragma unroll
             for (int i = 0; i < G; i++)
 #pragma unroll
                 for (int j = 0; j < TN; j++) {
                     t[i][j] = __dadd_rn(FIRST ? 0.0 : acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j]));
-                    acc[i0 + i][j] = R::fast(t[i][j]);
-                    ok = ok & R::ok(acc[i0 + i][j]);
+                    acc[i0 + i][j] =
+                        R::step(t[i][j], FIRST ? 0 : __double2loint(acc[i0 + i][j]), u[i][j]);
                 }
-            if (!ok) {  // rare: round these eight sums exactly
+#pragma unroll
+            for (int i = 0; i < G; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j += 2) run = R::fold2(run, u[i][j], u[i][j + 1]);
+            if (!R::valid(run)) {  // rare: round these sums exactly
 #pragma unroll
                 for (int i = 0; i < G; i++)
 #pragma unroll
@@ -196,14 +177,33 @@ __device__ __forceinline__ void blocked_fold(double (&tot)[TM][TN], double (&acc
         }
 }
 
-// Pairwise combine of the stack top with the current node (Dot.java:97-101).
+// Pairwise combine of the stack top with the current node (Dot.java:97-101):
+// right = round(left + right), validated in groups of GROUP_ROWS rows.
 template <int ACC, int RM>
 __device__ __forceinline__ void combine(const double (&left)[TM][TN], double (&right)[TM][TN]) {
+    using R = AccRound<ACC, RM>;
 #pragma unroll
-    for (int i = 0; i < TM; i++)
+    for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
+        double t[GROUP_ROWS][TN];
+        unsigned run = 0, u[GROUP_ROWS][TN];
 #pragma unroll
-        for (int j = 0; j < TN; j++) right[i][j] = __dadd_rn(left[i][j], right[i][j]);
-    round16<ACC, RM>(right);
+        for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++) {
+                t[i][j] = __dadd_rn(left[i0 + i][j], right[i0 + i][j]);
+                right[i0 + i][j] = R::step(t[i][j], __double2loint(right[i0 + i][j]), u[i][j]);
+            }
+#pragma unroll
+        for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j += 2) run = R::fold2(run, u[i][j], u[i][j + 1]);
+        if (!R::valid(run)) {
+#pragma unroll
+            for (int i = 0; i < GROUP_ROWS; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) right[i0 + i][j] = R::exact(t[i][j]);
+        }
+    }
 }
 
 // One 18 x 64 box of doubles (k0 .. k0+17 of rows r0 .. r0+63) into a tile.

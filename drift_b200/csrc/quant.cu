@@ -18,6 +18,7 @@
 // CTA counts into offsets (and advances the stored Rng state by the total),
 // and the apply pass recomputes each element's rank from the item counts and
 // a warp ballot. No kernel waits on another CTA, so nothing can spin.
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -95,22 +96,23 @@ struct QuantOp {
     __device__ bool needs_draw(const Item &it, double x, int &err) const {
         if (it.zero) return false;
         bool drew;
-        encode_value(f, scaled(it, x), DRIFT_STOCHASTIC, 0, drew, err);
+        quantize_value(f, scaled(it, x), DRIFT_STOCHASTIC, 0, drew, err);
         return drew;
     }
-    __device__ void apply(const Item &it, int64_t i, double x, uint64_t u53, bool &clamp,
-                          int &err) const {
-        if (it.zero) {
-            dst[i] = 0.0;
-            return;
-        }
+    // The cast of one element: what Quant.quantize stores (Quant.java:56-123).
+    __device__ double value(const Item &it, double x, uint64_t u53, bool &clamp, int &err) const {
+        if (it.zero) return 0.0;
         const double s = scaled(it, x);
         clamp = fabs(s) > f.max_finite;  // counted before rounding (Quant.java:67, :75, :117)
         bool drew;
-        double q = decode_value(f, encode_value(f, s, rm, u53, drew, err));
+        double q = quantize_value(f, s, rm, u53, drew, err);
         if (scaling == DRIFT_PER_TENSOR) q = __dmul_rn(q, inv);  // Quant.java:76
         else if (scaling == DRIFT_MX_BLOCK) q = __dmul_rn(q, it.up);  // exact, Quant.java:119
-        dst[i] = canon_nan(q);
+        return canon_nan(q);
+    }
+    __device__ void apply(const Item &it, int64_t i, double x, uint64_t u53, bool &clamp,
+                          int &err) const {
+        dst[i] = value(it, x, u53, clamp, err);
     }
 };
 
@@ -262,6 +264,100 @@ __global__ void __launch_bounds__(kThreads) elem_kernel(Op op_in, int64_t n, int
         if (lane == 0 && clamps) atomicAdd(sr.clamped, (unsigned long long)clamps);
     }
     if (err) atomicOr(sr.err, err);
+}
+
+// The single pass of a nearest-even or truncating cast when both arrays are
+// 16-byte aligned and items are 32 elements (no scaling, per-tensor, or MX
+// blocks of 32). A warp takes 128 consecutive elements per step as two
+// coalesced 512-byte loads (lane l holds elements 2l, 2l+1 and 64+2l,
+// 65+2l), so sixteen lanes hold one 32-element MX block and its amax is four
+// shuffles. The grid strides over the array; the clamp count is reduced once
+// per warp at the end.
+template <int SCALING>
+__global__ void __launch_bounds__(kThreads) cast_vec_kernel(QuantOp op_in, int64_t n,
+                                                            unsigned long long *clamped,
+                                                            int *err_out) {
+    QuantOp op = op_in;
+    op.prepare();
+    const int lane = threadIdx.x & 31;
+    const int64_t warp0 = ((int64_t)blockIdx.x * kThreads + threadIdx.x - lane) * 4;
+    const int64_t step = (int64_t)gridDim.x * kThreads * 4;
+    int err = 0;
+    unsigned clamps = 0;
+    for (int64_t base = warp0; base < n; base += step) {
+        double x[4];
+        int64_t at[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            at[h] = base + 64 * h + 2 * lane;
+            if (at[h] + 1 < n) {
+                const double2 v = __ldcs(reinterpret_cast<const double2 *>(op.src + at[h]));
+                x[2 * h] = v.x;
+                x[2 * h + 1] = v.y;
+            } else {
+                x[2 * h] = at[h] < n ? __ldcs(op.src + at[h]) : 0.0;
+                x[2 * h + 1] = 0.0;
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            QuantOp::Item it{1.0, 1.0, false};
+            if (SCALING == DRIFT_MX_BLOCK) {
+                // Quant.amax over the block (Quant.java:25-34): NaN never wins,
+                // and lanes past the end hold 0.
+                double m = fmax(fabs(x[2 * h]), fabs(x[2 * h + 1]));
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) m = fmax(m, __shfl_xor_sync(0xffffffffu, m, o));
+                if (m == 0.0 || !isfinite(m)) {  // Quant.java:105-110
+                    it.zero = true;
+                } else {
+                    const int sh = max(-127, min(127, java_get_exponent(m) - op.f.emax + op.headroom));
+                    it.down = pow2(-sh);
+                    it.up = pow2(sh);
+                }
+            }
+            bool c0 = false, c1 = false;
+            const double q0 = op.value(it, x[2 * h], 0, c0, err);
+            const double q1 = op.value(it, x[2 * h + 1], 0, c1, err);
+            if (at[h] + 1 < n) {
+                *reinterpret_cast<double2 *>(op.dst + at[h]) = make_double2(q0, q1);
+                clamps += c0 + c1;
+            } else if (at[h] < n) {
+                op.dst[at[h]] = q0;
+                clamps += c0;
+            }
+        }
+    }
+    if (clamped) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) clamps += __shfl_xor_sync(0xffffffffu, clamps, o);
+        if (lane == 0 && clamps) atomicAdd(clamped, (unsigned long long)clamps);
+    }
+    if (err) atomicOr(err_out, err);
+}
+
+// Launches cast_vec_kernel when the call fits it; false leaves it to elem_kernel.
+static bool launch_cast_vec(const QuantOp &op, int64_t n, int64_t item_len,
+                            unsigned long long *d_clamped, int *d_err, cudaStream_t st) {
+    if (op.rm == DRIFT_STOCHASTIC || item_len != 32) return false;
+    if (((uintptr_t)op.src | (uintptr_t)op.dst) % 16 != 0) return false;
+    if (n <= 0) return true;
+    // One wave: the CTAs every SM holds at once, or fewer for small casts.
+    const int64_t need = (n + kThreads * 4 - 1) / (kThreads * 4);
+    auto launch = [&](auto kernel) {
+        int dev = 0, sms = 148, per_sm = 1;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0);
+        const int64_t wave = (int64_t)std::max(1, sms) * std::max(1, per_sm);
+        kernel<<<(unsigned)std::min(need, wave), kThreads, 0, st>>>(op, n, d_clamped, d_err);
+    };
+    switch (op.scaling) {
+        case DRIFT_PER_TENSOR: launch(cast_vec_kernel<DRIFT_PER_TENSOR>); break;
+        case DRIFT_MX_BLOCK: launch(cast_vec_kernel<DRIFT_MX_BLOCK>); break;
+        default: launch(cast_vec_kernel<DRIFT_SCALE_NONE>);
+    }
+    return true;
 }
 
 // One CTA turns per-CTA draw counts into exclusive offsets and advances the
@@ -416,6 +512,8 @@ int launch_quantize(Workspace &ws, const drift_policy *p, int fmt, int rm, const
     int64_t item_len = 0;
     const int rc = make_quant_op(p, fmt, rm, d_src, d_dst, d_scale, scale, &op, &item_len);
     if (rc) return rc;
+    if (launch_cast_vec(op, n, item_len, d_clamped, d_err, st))
+        return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
     return run_elem(ws, op, n, item_len, rm == DRIFT_STOCHASTIC, d_state, d_clamped, d_err, st);
 }
 

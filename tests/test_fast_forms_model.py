@@ -1,0 +1,150 @@
+"""CPU models of two device arithmetic forms, pinned against the oracle.
+
+1. The tiled contraction's fast accumulator rounding (FastForm in codec.cuh):
+   r = fma(D, -2^S, fma(D, 2^S, t)) with D = 1.5 * 2^e built from t's high
+   word and the previous accumulator value's low word, validated by one
+   unsigned running max of t's exponent word. On every sum the validation
+   admits, the result must equal Dot.round / (float) (Dot.java:54, :63,
+   :141-182), ties included, for every low word an accumulator can hold.
+
+2. The cast's value-domain form (quantize_value in codec.cuh): decode(encode(s))
+   computed as min(round(|s| * 2^(mant-e)) * 2^(e-mant), maxFinite) with the
+   sign, for every format, rounding mode and special value, with stochastic
+   rounding drawing for exactly the elements MiniFloat.encode draws for
+   (MiniFloat.java:156-221, :258-278).
+
+Each model is a numpy restatement of the device code's steps; fma(D, 2^S, t)
+is an exact product plus one rounded add, so numpy's float64 add restates it.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+
+def _pow2(k):
+    return ((np.asarray(k, dtype=np.int64) + 1023) << 52).view(np.float64)
+
+
+# ------------------------------------------------------------------ accumulator rounding
+
+def _fast_round(t, prev_lo, shift, lo_e, hi_e, trunc=False):
+    hi = (t.view(np.uint64) >> np.uint64(32)).astype(np.uint32)
+    dh = (hi & np.uint32(0x7FF00000)) | np.uint32(0x00080000)
+    run = (dh - np.uint32((lo_e << 20) | 0x80000)).astype(np.uint32)     # wraps below lo_e
+    valid = run <= np.uint32((hi_e - lo_e) << 20)
+    if trunc:
+        mask = np.uint32(~((1 << (shift - 32)) - 1) & 0xFFFFFFFF)
+        bits = ((hi & mask).astype(np.uint64) << np.uint64(32)) | prev_lo.astype(np.uint64)
+        return bits.view(np.float64), valid
+    d = ((dh.astype(np.uint64) << np.uint64(32)) | prev_lo.astype(np.uint64)).view(np.float64)
+    c = d * float(2 ** shift)                  # exact: a power-of-two scaling
+    with np.errstate(all="ignore"):
+        return (c + t) - c, valid               # one rounding, then an exact subtraction
+
+
+def _sums(rs, n, shift, e_lo, e_hi):
+    """Doubles across and beyond the accumulator's range, a third of them
+    exact ties at the target precision and a third within a few ulps of one."""
+    e = rs.integers(e_lo, e_hi, n)
+    m = rs.integers(0, 1 << 52, n, dtype=np.int64)
+    k = n // 3
+    m[:k] = (m[:k] >> shift << shift) | (1 << (shift - 1))
+    m[k:2 * k] = ((m[k:2 * k] >> shift << shift) | (1 << (shift - 1))) + rs.integers(-3, 4, k)
+    m &= (1 << 52) - 1
+    t = np.ldexp(1.0 + m / 2.0 ** 52, e) * np.where(rs.random(n) < 0.5, -1.0, 1.0)
+    t[:64] = 0.0
+    t[64:70] = [np.inf, -np.inf, np.nan, 5e-324, -1e-310, 1e300]
+    return t
+
+
+@pytest.mark.parametrize("acc", ["fp32", "fp16", "bf16"])
+def test_fast_accumulator_rounding_matches_oracle(acc):
+    rs = np.random.default_rng(11)
+    n = 600_000
+    if acc == "fp32":
+        shift, lo_e, hi_e = 29, 1023 - 126, 1023 + 126
+        t = _sums(rs, n, shift, -150, 130)
+        # Any float's low word: 0 or a multiple of 2^29.
+        prev_lo = rs.integers(0, 8, n).astype(np.uint32) << np.uint32(29)
+        with np.errstate(over="ignore"):
+            want = {0: t.astype(np.float32).astype(np.float64)}
+    else:
+        acc_id = 2 if acc == "fp16" else 3
+        mant, min_e, max_e = (10, -14, 15) if acc == "fp16" else (7, -126, 127)
+        shift, lo_e, hi_e = 52 - mant, 1023 + min_e, 1023 + max_e - 1
+        t = _sums(rs, n, shift, min_e - 10, max_e + 3)
+        prev_lo = np.zeros(n, np.uint32)            # FP16/BF16 values have a zero low word
+        want = {0: O.acc_round(acc_id, O.NEAREST_EVEN, t)[0],
+                2: O.acc_round(acc_id, O.TRUNCATE, t)[0]}
+    for rm, w in want.items():
+        got, valid = _fast_round(t, prev_lo, shift, lo_e, hi_e, trunc=rm == 2)
+        bad = valid & (got.view(np.int64) != w.view(np.int64))
+        assert not bad.any(), (acc, rm, t[bad][:3])
+        # The fast form takes nearly every in-range sum; zero, Inf, NaN and
+        # the subnormal range are always refused.
+        assert valid.mean() > 0.6
+        assert not valid[:70].any()
+
+
+# ------------------------------------------------------------------ cast values
+
+def _quantize_value(fmt, s, rm, u=None):
+    maxf, minn, minsub, _ = O.format_info(fmt)
+    mant = int(round(np.log2(minn / minsub)))
+    min_e = int(round(np.log2(minn)))
+    a = np.abs(s)
+    e = ((a.view(np.uint64) >> np.uint64(52)) & np.uint64(0x7FF)).astype(np.int64) - 1023
+    e = np.minimum(np.maximum(e, min_e), 1023)
+    drew = np.zeros(s.size, bool)
+    with np.errstate(all="ignore"):
+        sc = a * _pow2(mant - e)
+        if rm == O.NEAREST_EVEN:
+            m = (sc + 2.0 ** 52) - 2.0 ** 52
+        else:
+            m = np.floor(sc)
+            if rm == O.STOCHASTIC:
+                frac = sc - m
+                drew = (frac != 0) & (a < np.inf)
+                m = np.where(drew & (u < frac), m + 1, m)
+        q = np.copysign(np.fmin(m * _pow2(e - mant), maxf), s)
+    return np.where(np.isnan(s), np.nan, q), drew
+
+
+def _cast_inputs(rs, fmt):
+    maxf, _, _, width = O.format_info(fmt)
+    x = rs.standard_normal(200_000) * np.exp(rs.standard_normal(200_000) * 3) * maxf / 8
+    codes = (np.arange(1 << width, dtype=np.int32) if width <= 16
+             else rs.integers(0, 1 << 16, 20_000).astype(np.int32))
+    v = np.abs(O.decode(fmt, codes))
+    v = np.unique(v[np.isfinite(v)])
+    mids = (v[1:] + v[:-1]) / 2
+    return np.concatenate([x, v, -v, mids, -mids, np.nextafter(mids, 0), np.nextafter(mids, 9e9),
+                           [0.0, -0.0, 5e-324, -1e-310, 1e300, -1e300, np.inf, -np.inf, maxf,
+                            maxf * 1.0001, 2 * maxf, -2 * maxf]])
+
+
+@pytest.mark.parametrize("fmt", range(7))
+def test_value_domain_cast_matches_oracle(fmt):
+    rs = np.random.default_rng(100 + fmt)
+    x = _cast_inputs(rs, fmt)
+    if fmt not in (O.E2M1, O.E3M2, O.E2M3):          # formats with NaN
+        x = np.concatenate([x, [np.nan, -np.nan]])
+    for rm in (O.NEAREST_EVEN, O.TRUNCATE):
+        want, _, _ = O.quantize(O.policy(input_format=fmt), fmt, rm, x, 1.0)
+        got, _ = _quantize_value(fmt, x, rm)
+        same = (got.view(np.int64) == want.view(np.int64)) | (np.isnan(got) & np.isnan(want))
+        assert same.all(), (fmt, rm, x[~same][:3])
+    # Stochastic rounding: the model draws for the same elements, in order,
+    # and the Rng ends in the same state.
+    x = x[np.isfinite(x) | np.isinf(x)][:60_000]
+    _, drew = _quantize_value(fmt, x, O.STOCHASTIC, np.zeros(x.size))
+    u = np.zeros(x.size)
+    st = 0x5EED
+    for i in np.flatnonzero(drew):
+        u[i], st = O.rng_next_double(st)
+    got, _ = _quantize_value(fmt, x, O.STOCHASTIC, u)
+    want, _, want_st = O.quantize(O.policy(input_format=fmt, input_rounding=O.STOCHASTIC), fmt,
+                                  O.STOCHASTIC, x, 1.0, 0x5EED)
+    assert st == want_st
+    assert (got.view(np.int64) == want.view(np.int64)).all()
