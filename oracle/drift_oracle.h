@@ -80,6 +80,8 @@ double o_jrandom_next_double(o_jrandom *r);
 double o_jrandom_next_gaussian(o_jrandom *r);
 int32_t o_jrandom_next_int(o_jrandom *r, int32_t bound);
 /* DotSweep.fill(a, b, seed) (java/.../tools/DotSweep.java:124-130). */
+/* StrictMath.log: fdlibm 5.3's logarithm, restated (drift_oracle.c). */
+double o_strict_log(double x);
 void o_dotsweep_fill(double *a, double *b, int64_t n, int64_t seed);
 
 #ifdef __cplusplus
