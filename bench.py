@@ -246,19 +246,31 @@ def run_engine(args):
     def gemm_launches(k):
         return 5 if routes[k] in (d.ROUTE_FP32, d.ROUTE_SCANNED) else 1
 
-    def cast(p, src, dst, slot, counter):
+    # The cast pass's own device time (the quantize launch of each cast policy's
+    # A operand, last step), for its HBM roofline.
+    cast_ev = {k: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for k, p in enumerate(pols) if p.input_format is not None}
+
+    def cast(p, src, dst, slot, counter, k=None):
         f = p.input_format
         if f is None:
             return src
+        timed = k in cast_ev and slot == 0
         if p.scaling == d.Scaling.PER_TENSOR:
             d.amax_dev(src, scal[slot:slot + 1], ctx=ctx)
             d.per_tensor_scale_dev(f, scal[slot:slot + 1], scal[2 + slot:3 + slot], ctx=ctx)
+            if timed:
+                cast_ev[k][0].record(stream)
             d.quantize_dev(p, f, p.input_rounding, src, dst, d_scale=scal[2 + slot:3 + slot],
                            d_clamped=counter, ctx=ctx)
             launches[0] += 3
         else:
+            if timed:
+                cast_ev[k][0].record(stream)
             d.quantize_dev(p, f, p.input_rounding, src, dst, d_clamped=counter, ctx=ctx)
             launches[0] += 1
+        if timed:
+            cast_ev[k][1].record(stream)
         return dst
 
     def step(read_routes: bool):
@@ -269,7 +281,7 @@ def run_engine(args):
             routes[0] = d.gemm_route(ctx=ctx)
         launches[0] += gemm_launches(0)
         for k, p in enumerate(pols):
-            a = cast(p, A, qA, 0, clamps[k, 0:1])
+            a = cast(p, A, qA, 0, clamps[k, 0:1], k)
             b = cast(p, B, qB, 1, clamps[k, 1:2])
             ev[k + 1][0].record(stream)
             d.gemm_dev(p, a, b, C, ctx=ctx)
@@ -347,6 +359,13 @@ def run_engine(args):
     except (OSError, KeyError, ValueError):
         pass
     hbm_gbs = traffic_per_launch * len(on_fp64) / (gemm_total_ms * 1e-3) / 1e9
+    # The cast pass (cast_vec_kernel): 8 bytes read and 8 written per element.
+    cast_bytes = 16 * M * K
+    cast_line = {}
+    for k, (e0, e1) in cast_ev.items():
+        ms = e0.elapsed_time(e1)
+        cast_line[pols[k].name] = {"ms": ms, "achieved": cast_bytes / (ms * 1e-3) / 1e9,
+                                   "frac": cast_bytes / (ms * 1e-3) / 1e9 / hbm_peak}
     per_policy = {"exact fp64": M * N * K / (gemm_ms[0] * 1e-3)}
     for k, p in enumerate(pols):
         per_policy[p.name] = M * N * K / (gemm_ms[k + 1] * 1e-3)
@@ -408,7 +427,12 @@ def run_engine(args):
                                    "peak_source": "measured FFMA probe (drift_probe_fp32) on "
                                                   "this GPU",
                                    "note": "one FFMA per emulated MAC; the time includes the "
-                                           "operand scans and the decision"}},
+                                           "operand scans and the decision"},
+                     "cast_pass": {"kernel": "cast_vec_kernel", "bound": "hbm", "unit": "GB/s",
+                                   "peak": hbm_peak, "peak_source": hbm_src,
+                                   "bytes_per_element": 16, "per_policy": cast_line,
+                                   "note": "the quantize launch of one 8192 x 8192 operand, "
+                                           "CUDA events on the launching stream, last step"}},
         "per_policy_mac_per_s": per_policy,
         "stats": stats,
         "e2e": e2e,
@@ -669,47 +693,187 @@ def run_train(args):
     return 0
 
 
+def _cpu_dot_sweep(inputs, policies, threads):
+    """The dot sweep on the oracle (the C restatement of DotSweep.run,
+    DotSweep.java:112-122) over the given vectors: (policy, length) groups in
+    parallel on `threads` host threads. Returns seconds."""
+    import concurrent.futures as cf
+    from oracle import oracle as O
+
+    def opol(p):
+        c = p.to_c()
+        return O.OraclePolicy(*[getattr(c, f) for f, _ in c._fields_])
+
+    exact = O.policy(acc=O.ACC_FP64)
+
+    def group(p, n):
+        op = opol(p)
+        f = p.input_format
+        fid = f.id if f is not None else -1
+        A, B = inputs[n]
+        for seed in range(A.shape[0]):
+            a, b = A[seed], B[seed]
+            rng = 0xD1F7 + seed
+            if f is not None:
+                sa = O.per_tensor_scale(fid, O.amax(a))
+                sb = O.per_tensor_scale(fid, O.amax(b))
+                a, _, rng = O.quantize(op, fid, int(p.input_rounding), a, sa, rng)
+                b, _, rng = O.quantize(op, fid, int(p.input_rounding), b, sb, rng)
+            O.dot(a, 0, 1, b, 0, 1, n, op, rng)
+            O.dot(A[seed], 0, 1, B[seed], 0, 1, n, exact)
+
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda pn: group(*pn), [(p, n) for p in policies for n in inputs]))
+    return time.perf_counter() - t0
+
+
+def _cpu_real_dot(X, W, policies, threads):
+    """The real-shape batch on the oracle with `threads` host threads: casts,
+    every contraction, the medians and RMS sums. Returns seconds."""
+    import numpy as np
+    from oracle import oracle as O
+
+    def opol(p):
+        c = p.to_c()
+        return O.OraclePolicy(*[getattr(c, f) for f, _ in c._fields_])
+
+    t0 = time.perf_counter()
+    M, K = X.shape
+    N = W.shape[0]
+    xf, wf = X.reshape(-1), W.reshape(-1)
+    exact, _ = O.gemm(O.policy(acc=O.ACC_FP64), M, N, K, xf, 0, K, 1, wf, 0, K, 1,
+                      threads=threads)
+    for p in policies:
+        f = p.input_format
+        qx, qw, rng = xf, wf, 7
+        if f is not None:
+            qx, _, rng = O.quantize(opol(p), f.id, 0, xf, O.per_tensor_scale(f.id, O.amax(xf)),
+                                    rng)
+            qw, _, rng = O.quantize(opol(p), f.id, 0, wf, O.per_tensor_scale(f.id, O.amax(wf)),
+                                    rng)
+        got, _ = O.gemm(opol(p), M, N, K, qx, 0, K, 1, qw, 0, K, 1, threads=threads)
+        err = np.abs(got - exact).reshape(-1) / np.abs(exact).reshape(-1)
+        np.partition(err, [err.size // 2 - 1, err.size // 2])
+        np.sqrt(np.sum((got - exact) ** 2) / np.sum(exact ** 2))
+    return time.perf_counter() - t0
+
+
 def run_configs(args):
     """The other study configurations, timed end to end on one GPU (inputs
-    generated first, results read back): the dot sweep (200 seeds x lengths
-    16..4096, 10 policies + exact), the real-shape batch (4096 x 64 x 2048,
-    7 policies + exact) and the block-scaled GEMM (4096^3, 6 policies +
-    exact). Wall-clock seconds, emulated MACs and MAC/s, with each study's
-    headline figures."""
+    generated or copied in, results read back), each beside the oracle on
+    the host's threads over the same work: the dot sweep (200 seeds x lengths
+    16..4096, 10 policies + exact, inputs generated on the device), the
+    real-shape batch (4096 x 64 x 2048, 7 policies + exact, the host tensors
+    copied in once) and the block-scaled GEMM (4096^3, 6 policies + exact; the
+    CPU leg is a 16-row sample, scaled to the whole study)."""
+    import statistics as stt
+
+    import numpy as np
     import torch
     from drift_b200 import sweeps
+    from oracle import oracle as O
 
-    out = {}
+    threads = os.cpu_count() or 1
+    out = {"cpu_threads": threads}
+    reps = max(1, args.steps)
+
+    def timed(fn):
+        fn()   # warm-up, the same call
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            r = fn()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t0)
+        return stt.median(ts), r
+
     lengths = tuple(2 ** k for k in range(4, 13))
-    sweeps.dot_sweep_dev(lengths=(16,), seeds=2)   # warm-up
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    ds = sweeps.dot_sweep_dev(lengths=lengths, seeds=200)
-    torch.cuda.synchronize()
-    dt = time.perf_counter() - t0
+    dt, ds = timed(lambda: sweeps.dot_sweep_dev(lengths=lengths, seeds=200))
     macs = 11 * 200 * sum(lengths)
-    t = ds["table"]
+    inputs = sweeps.dot_sweep_dev(lengths=lengths, seeds=200, keep_inputs=True)["inputs"]
+    cpu = _cpu_dot_sweep(inputs, sweeps.dot_sweep_policies(), threads)
     out["dot_sweep"] = {"seconds": dt, "macs": macs, "mac_per_s": macs / dt,
+                        "cpu_port_seconds": cpu, "vs_cpu_port": cpu / dt,
+                        "path": "device: inputs generated on the GPU, one read-back",
                         "median_rel_error_at_4096": {k: v[4096]["median_rel_error"]
-                                                      for k, v in t.items()}}
+                                                      for k, v in ds["table"].items()}}
     X, W = sweeps.real_dot_inputs()
-    sweeps.real_dot_batch(X[:64], W)   # warm-up
-    t0 = time.perf_counter()
-    rd = sweeps.real_dot_batch(X, W)
-    dt = time.perf_counter() - t0
+    dt, rd = timed(lambda: sweeps.real_dot_batch_dev(X, W))
     macs = 8 * X.shape[0] * W.shape[0] * X.shape[1]
+    cpu = _cpu_real_dot(X, W, sweeps.real_dot_policies(), threads)
     out["real_dot_batch"] = {"seconds": dt, "macs": macs, "mac_per_s": macs / dt,
-                             "path": "host-buffer entry points", "stats": rd}
-    sweeps.mx_gemm(512)   # warm-up
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    mx = sweeps.mx_gemm(4096)
-    torch.cuda.synchronize()
-    dt = time.perf_counter() - t0
+                             "cpu_port_seconds": cpu, "vs_cpu_port": cpu / dt,
+                             "path": "device: host X and W copied in once, one read-back",
+                             "stats": rd}
+    dt, mx = timed(lambda: sweeps.mx_gemm(4096))
     macs = 7 * 4096 ** 3
+    A, Wm = (t.cpu().numpy() for t in sweeps.mx_gemm_inputs(4096))
+    rows = 16
+    t0 = time.perf_counter()
+    for p in [sweeps.NumericPolicy.exact()] + sweeps.mx_policies():
+        c = p.to_c()
+        op = O.OraclePolicy(*[getattr(c, f) for f, _ in c._fields_])
+        a, w = A[:rows].reshape(-1), Wm.reshape(-1)
+        if p.input_format is not None:
+            fid = p.input_format.id
+            sa = O.per_tensor_scale(fid, O.amax(A)) if p.scaling == 1 else 1.0
+            sw = O.per_tensor_scale(fid, O.amax(Wm)) if p.scaling == 1 else 1.0
+            a = O.quantize(op, fid, 0, a, sa)[0]
+            w = O.quantize(op, fid, 0, w, sw)[0]
+        O.gemm(op, rows, 4096, 4096, a, 0, 4096, 1, w, 0, 4096, 1, threads=threads)
+    cpu = (time.perf_counter() - t0) * 4096 / rows
     out["mx_gemm"] = {"seconds": dt, "macs": macs, "mac_per_s": macs / dt,
+                      "cpu_port_seconds_extrapolated": cpu, "vs_cpu_port": cpu / dt,
                       "path": "device-resident", "stats": mx}
     print(json.dumps({"mode": "configs", **out}), flush=True)
+    return 0
+
+
+def run_mx(args):
+    """The block-scaled GEMM study (M = N = K = size, e4m3/e2m1 x per-tensor /
+    MX spec / MX +1, FP32 sequential, plus the exact GEMM) as one job over N
+    ranks, each GEMM sharded by N-tile: per-GPU work shrinks as ranks are added
+    (strong scaling). Device time of the whole study (casts, contractions,
+    statistics) per step, max over ranks."""
+    import torch
+    import drift_b200 as d
+    from drift_b200 import dist as ddist
+    from drift_b200 import sweeps
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    d.Context.use_device(local)
+    pg = None
+    if world > 1:
+        pg = ddist.init("nccl", timeout_s=600, device=torch.device("cuda", local))
+    S = args.size
+    inputs = sweeps.mx_gemm_inputs(S, 0, local)
+    for _ in range(args.warmup):
+        res = sweeps.mx_gemm(S, dist=pg, inputs=inputs, device=local)
+    torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        res = sweeps.mx_gemm(S, dist=pg, inputs=inputs, device=local)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = ddist.max_over_ranks(e0.elapsed_time(e1), pg, torch.device("cuda", local))
+    n_gemm = 1 + len(sweeps.mx_policies())
+    macs = n_gemm * S ** 3 * args.steps
+    ddist.finish(pg)
+    if rank == 0:
+        print(json.dumps({"mode": "mx", "metric": UNIT, "value": macs / (ms * 1e-3), "unit": UNIT,
+                          "n_gpus": world, "steps": args.steps, "ms_per_step": ms / args.steps,
+                          "scaling": "strong",
+                          "config": {"workload": f"block-scaled GEMM study M=N=K={S}, "
+                                                 f"{n_gemm - 1} policies + exact, one study per "
+                                                 f"step sharded by N-tile over {world} ranks"},
+                          "stats": res}), flush=True)
     return 0
 
 
@@ -723,7 +887,7 @@ def main() -> int:
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", choices=["sweep", "kernels", "train", "configs"], default="sweep",
+    ap.add_argument("--mode", choices=["sweep", "kernels", "train", "configs", "mx"], default="sweep",
                     help="kernels: time each policy's contraction alone (for profiling)")
     ap.add_argument("--policies", default="", help="kernels mode: comma-separated policy names")
     ap.add_argument("--mnk", default="", help="kernels mode: M,N,K instead of size^3")
@@ -738,6 +902,8 @@ def main() -> int:
         return run_train(args)
     if args.mode == "configs":
         return run_configs(args)
+    if args.mode == "mx":
+        return run_mx(args)
     return run_engine(args)
 
 

@@ -96,6 +96,7 @@ SIGNATURES = {
     "drift_error_sums_dev": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "drift_radix_hist_dev": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp]),
     "drift_radix_select_dev": (_int, [_vp, _int, _vp, _vp, _vp]),
+    "drift_group_kth_rel_error_dev": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "drift_embed_gather_dev": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "drift_embed_grad_dev": (_int, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp]),
     "drift_bias_grad_dev": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),

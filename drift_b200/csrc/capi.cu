@@ -914,6 +914,18 @@ int drift_radix_select_dev(drift_ctx *ctx, int pass, const uint64_t *d_hist, uin
     return rc ? fail(rc, "radix select") : DRIFT_OK;
 }
 
+int drift_group_kth_rel_error_dev(drift_ctx *ctx, const double *d_got, const double *d_exact,
+                                  int64_t groups, int64_t n, int64_t k, double *d_out,
+                                  void *stream) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (groups < 0 || (groups > 0 && (!d_got || !d_exact || !d_out)))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    rc = launch_group_kth(d_got, d_exact, groups, n, k, d_out, pick(ctx, stream));
+    return rc ? fail(rc, "per-group order statistic (n <= DRIFT_GROUP_MAX, 0 <= k < n)")
+              : DRIFT_OK;
+}
+
 int drift_probe_fp64(drift_ctx *ctx, double *ops_per_s) {
     int rc = enter(ctx);
     if (rc) return rc;

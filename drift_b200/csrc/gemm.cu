@@ -66,6 +66,18 @@ constexpr int STAGE_DOUBLES = (BM + BN) * LDK;   // one A tile and one B tile
 constexpr int TILE_BYTES = BM * LDK * (int)sizeof(double);  // 9 KiB per operand per stage
 // Stages plus the stage barriers.
 constexpr int GEMM_SMEM = STAGES * STAGE_DOUBLES * (int)sizeof(double) + 64;
+// Pairwise leaves over a full tile are validated once per tile (mac16_run,
+// one check, the two leaves redone exactly from zero on a miss) for the FP32
+// and BF16 accumulators. Measured at 8192^3 on one B200: FP32 pairwise +8%.
+// Not for FP16, whose normal range starts at 2^-14: a leaf starts from one
+// product, and small products fall below it often enough that a large share
+// of tiles would be redone (2.5x slower); nor for the sequential and blocked
+// orders, which lost 4-5% with a tile-start copy of the accumulators in
+// shared memory to restart from.
+template <int ACC, int ORDER>
+constexpr bool tile_validated() {
+    return ORDER == DRIFT_PAIRWISE && (ACC == DRIFT_ACC_FP32 || ACC == DRIFT_ACC_BF16);
+}
 constexpr int kMaxPairwiseDepth = 30;  // stack depth; enough for any int32 K
 // Unroll of the k-pair loop of a full tile, chosen by measurement on B200:
 // the narrow accumulators' rounding makes a long tile body fall out of the
@@ -160,6 +172,49 @@ __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[T
                     for (int j = 0; j < TN; j++) acc[i0 + i][j] = R::exact(t[i][j]);
             }
         }
+    }
+}
+
+// One k step of a full tile: as mac16, but the sums' range words are folded
+// into `run`, which the caller checks once for the whole tile. No sum is kept
+// for a recompute: a tile that misses is redone from its start (redo_*).
+template <int ACC, int RM, bool FIRST = false>
+__device__ __forceinline__ void mac16_run(double (&acc)[TM][TN], const double (&a)[TM],
+                                          const double (&b)[TN], unsigned &run) {
+    using R = AccRound<ACC, RM>;
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        unsigned u[TN];
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const double t = __dadd_rn(FIRST ? 0.0 : acc[i][j], __dmul_rn(a[i], b[j]));
+            acc[i][j] = R::step(t, FIRST ? 0 : __double2loint(acc[i][j]), u[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < TN; j += 2) run = R::fold2(run, u[j], u[j + 1]);
+    }
+}
+
+// A tile's k steps [k0, k1) (in reverse when REV) with the exact rounding,
+// into acc (Dot.java:50-68): the rare path of a tile whose fast steps left the
+// accumulator's normal range. The tile is still in shared memory.
+template <int ACC, int RM, bool REV>
+__device__ __forceinline__ void redo_steps(const double *sA, const double *sB, int ty, int tx,
+                                           int k0, int k1, double (&acc)[TM][TN]) {
+    using R = AccRound<ACC, RM>;
+#pragma unroll 1
+    for (int q = k0; q < k1; q++) {
+        const int kk = REV ? k1 - 1 - (q - k0) : q;
+        double a[TM], b[TN];
+#pragma unroll
+        for (int i = 0; i < TM; i++) a[i] = sA[tile_off(ty + 16 * i, kk)];
+#pragma unroll
+        for (int j = 0; j < TN; j++) b[j] = sB[tile_off(tx + 16 * j, kk)];
+#pragma unroll
+        for (int i = 0; i < TM; i++)
+#pragma unroll
+            for (int j = 0; j < TN; j++)
+                acc[i][j] = R::exact(__dadd_rn(acc[i][j], __dmul_rn(a[i], b[j])));
     }
 }
 
@@ -354,7 +409,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
 
         if (SEG != SEG_SCHED && kn == BK) {
             // A full tile, no per-k segment work: two k per 16-byte read.
+            // Tile-validated kernels fold the range words of the whole tile
+            // into `run` and check it once (a miss redoes the leaves exactly);
+            // the others validate each k step's groups (mac16).
+            using R = AccRound<ACC, RM>;
+            constexpr bool TV = tile_validated<ACC, ORDER>();
             constexpr int G = mac_group<ORDER>();
+            unsigned run = 0;
             auto kpair = [&](int q, double(&dst)[TM][TN], auto first) {
                 const int kp = REV ? BK / 2 - 1 - q : q;
                 double2 a2[TM], b2[TN];
@@ -369,13 +430,25 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
                 const double bx[TN] = {b2[0].x, b2[1].x, b2[2].x, b2[3].x};
                 const double by[TN] = {b2[0].y, b2[1].y, b2[2].y, b2[3].y};
                 constexpr bool F = decltype(first)::value;
-                if (REV) {
+                if constexpr (TV) {
+                    mac16_run<ACC, RM, F>(dst, ax, bx, run);
+                    mac16_run<ACC, RM>(dst, ay, by, run);
+                } else if (REV) {
                     mac16<ACC, RM, G, F>(dst, ay, by);
                     mac16<ACC, RM, G>(dst, ax, bx);
                 } else {
                     mac16<ACC, RM, G, F>(dst, ax, bx);
                     mac16<ACC, RM, G>(dst, ay, by);
                 }
+            };
+            // The tile's two pairwise leaves of 8 from zero, exactly.
+            auto redo_leaves = [&](double(&l0)[TM][TN], double(&l1)[TM][TN]) {
+#pragma unroll
+                for (int i = 0; i < TM; i++)
+#pragma unroll
+                    for (int j = 0; j < TN; j++) l0[i][j] = l1[i][j] = 0.0;
+                redo_steps<ACC, RM, false>(sA, sB, ty, tx, 0, BK / 2, l0);
+                redo_steps<ACC, RM, false>(sA, sB, ty, tx, BK / 2, BK, l1);
             };
             using Fresh = std::integral_constant<bool, true>;
             using Cont = std::integral_constant<bool, false>;
@@ -392,6 +465,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
                 kpair(BK / 4, acc, Fresh{});
 #pragma unroll 1
                 for (int q = BK / 4 + 1; q < BK / 2; q++) kpair(q, acc, Cont{});
+                if (TV && !R::valid(run)) redo_leaves(leaf0, acc);
                 combine<ACC, RM>(leaf0, acc);
                 push(__ffsll(t + 1) - 1, true);    // ctz(t+1) merges in a perfect tree
             } else {
@@ -411,6 +485,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
                                 }
                         }
                     }
+                }
+                if constexpr (TV && PAIR && SEG == SEG_TILE) {
+                    if (!R::valid(run)) redo_leaves(leaf0, acc);  // rare
                 }
                 if constexpr (PAIR && SEG == SEG_TILE) {
                     combine<ACC, RM>(leaf0, acc);   // the tile's level-1 node

@@ -73,6 +73,8 @@ int launch_error_sums(const double *got, const double *exact, int64_t n, double 
                       cudaStream_t st);
 int launch_radix_pass(const double *got, const double *exact, int64_t n, int pass,
                       unsigned long long *state, unsigned long long *hist, cudaStream_t st);
+int launch_group_kth(const double *got, const double *exact, int64_t groups, int64_t n,
+                     int64_t k, double *out, cudaStream_t st);
 int launch_radix_select(int pass, const unsigned long long *hist, unsigned long long *state,
                         cudaStream_t st);
 // contract.cu: a contraction with its buffers (a, b, c before the op's

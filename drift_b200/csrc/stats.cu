@@ -140,4 +140,52 @@ int launch_radix_select(int pass, const unsigned long long *hist, unsigned long 
     return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 
+// ------------------------------------------------------------------ per-group order statistics
+//
+// The dot sweep reports, per (policy, length), the upper median of a few
+// hundred relative errors (DotSweep.java:152-153). Here every group is one
+// CTA: its keys (the relative errors' bit patterns, NaN above +Inf, as in
+// radix selection) are sorted in shared memory by a bitonic network padded
+// to a power of two with the largest key, and element k is written out as a
+// double. Groups of up to kGroupMax elements.
+
+constexpr int kGroupMax = 4096;
+
+__global__ void __launch_bounds__(1024) group_kth_kernel(const double *got, const double *exact,
+                                                         int64_t n, int64_t k, double *out) {
+    __shared__ uint64_t keys[kGroupMax];
+    const int64_t g = blockIdx.x;
+    int m = 1;
+    while (m < n) m <<= 1;
+    for (int i = threadIdx.x; i < m; i += blockDim.x)
+        keys[i] = i < n ? rel_error_key(got[g * n + i], exact[g * n + i]) : ~0ULL;
+    __syncthreads();
+    for (int size = 2; size <= m; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < m; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool up = (i & size) == 0;
+                    const uint64_t a = keys[i], b = keys[j];
+                    if ((a > b) == up) {
+                        keys[i] = b;
+                        keys[j] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x == 0) out[g] = bitsd(keys[k]);
+}
+
+int launch_group_kth(const double *got, const double *exact, int64_t groups, int64_t n,
+                     int64_t k, double *out, cudaStream_t st) {
+    if (groups < 0 || n <= 0 || n > kGroupMax || k < 0 || k >= n || groups > 0x7fffffffLL)
+        return DRIFT_EINVAL;
+    if (groups == 0) return DRIFT_OK;
+    group_kth_kernel<<<(unsigned)groups, 1024, 0, st>>>(got, exact, n, k, out);
+    return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
+}
+
 }  // namespace drift

@@ -284,3 +284,28 @@ def sharded_gemm(p, A_rows, B, C_rows, state: int, dist=None, *, bias=None,
         settled.append(counts[r])
     last_gemm_rounds = max_rounds + world
     return advance(state, sum(settled))
+
+
+# ------------------------------------------------------------------ N-tile sharded GEMM
+
+def ntile_bounds(N: int, world: int, rank: int, tile: int = 64):
+    """Output columns [lo, hi) of `rank`'s N-tile shard: contiguous, balanced,
+    on the contraction's 64-wide tile boundaries."""
+    return shard_bounds(N, world, rank, tile)
+
+
+def ntile_gemm(p, A, B_cols, C_cols, *, bias_cols=None) -> None:
+    """One GEMM sharded by N-tile: every rank holds all of A and the rows
+    [lo, hi) of B (ntile_bounds; B's rows are C's columns) and writes
+    C[:, lo:hi], which `C_cols` may view inside a full C (any row stride).
+    Each output is its own dot over A's row and B's row, so no operand
+    crosses ranks and the contraction needs no collective; the callers reduce
+    only statistics. A stochastic accumulator draws in (i, o) order, which
+    interleaves the ranks' columns row by row, so it is refused here:
+    sharded_gemm splits by rows and settles the draw offsets."""
+    from .kernel import gemm_dev
+
+    if stochastic_acc(p):
+        raise ValueError("ntile_gemm: a stochastic accumulator draws in (i, o) order across "
+                         "the column shards; use sharded_gemm (row blocks)")
+    gemm_dev(p, A, B_cols, C_cols, c_rs=C_cols.stride(0), bias=bias_cols)

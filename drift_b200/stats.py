@@ -62,3 +62,13 @@ def true_median_rel_error(got, exact, total: int, dist=None, **kw) -> float:
     lo = kth_rel_error(got, exact, total // 2 - 1, dist, **kw)
     hi = kth_rel_error(got, exact, total // 2, dist, **kw)
     return 0.5 * (lo + hi)
+
+
+def group_kth_rel_error_dev(got, exact, groups: int, n: int, k: int, out, stream=None,
+                            ctx=None) -> None:
+    """out[g] = the k-th smallest (0-based) relative error within group g of
+    n consecutive outputs (n <= 4096), for `groups` groups in one launch."""
+    ctx = ctx or _lib.Context.current()
+    _lib.check(_lib.load().drift_group_kth_rel_error_dev(ctx.handle, _tptr(got), _tptr(exact),
+                                                         groups, n, k, _tptr(out),
+                                                         _stream_ptr(stream)))

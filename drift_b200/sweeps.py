@@ -104,68 +104,109 @@ def dot_sweep(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)), seed
     return {"table": table, "rows": rows}
 
 
+def dot_sweep_inputs_dev(n: int, seeds: int, sigma: float = 1.0, device: int = 0):
+    """The dot sweep's vectors of length n for every seed, generated on the
+    device: two seeds x n tensors of fp32 N(0,1) x lognormal(0, sigma) values
+    held as doubles (row s is seed s's vector), seeded by n."""
+    import torch
+
+    dev = torch.device("cuda", device)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7919 + n)
+    out = []
+    for _ in range(2):
+        x = torch.randn(seeds, n, device=dev, generator=g)
+        x *= torch.exp(torch.randn(seeds, n, device=dev, generator=g) * sigma)
+        out.append(x.double())
+    return out[0], out[1]
+
+
 def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
                   seeds: int = 200, policies: Optional[List[NumericPolicy]] = None,
-                  sigma: float = 1.0, device: int = 0) -> Dict:
-    """dot_sweep with every dot of one (policy, length) in one batched
-    contraction on the device: the seeds' vectors are the rows of two
-    seeds x n tensors and the dots a batch of 1 x 1 contractions. The casts
-    follow DotSweep.run (DotSweep.java:112-122) per seed: the vector's own
-    per-tensor scale, a then b on the seed's Rng(0xD1F7 + seed). Same inputs,
-    outputs and rows as dot_sweep."""
+                  sigma: float = 1.0, device: int = 0, host_inputs: bool = False,
+                  keep_inputs: bool = False) -> Dict:
+    """The dot sweep on the device. The seeds' vectors are the rows of two
+    seeds x n tensors and each (policy, length) is one batched contraction of
+    1 x 1 dots. The casts follow DotSweep.run (DotSweep.java:112-122) per
+    seed: the vector's own per-tensor scale, a then b on the seed's
+    Rng(0xD1F7 + seed). Every value and clamp count lands in one device
+    array, the per-(policy, length) upper medians (DotSweep.java:152-153)
+    come from one launch, and everything is read back once at the end.
+
+    Inputs are generated on the device (dot_sweep_inputs_dev), or with
+    host_inputs on the host exactly as dot_sweep draws them (the same rows as
+    dot_sweep then). keep_inputs returns the vectors too, for checking."""
     import torch
 
     from .kernel import (amax_dev, check_dev, contract_dev, contraction, per_tensor_scale_dev,
                          quantize_dev, quantize_rows_dev)
+    from .stats import group_kth_rel_error_dev
 
     policies = policies or dot_sweep_policies()
     dev = torch.device("cuda", device)
     exact_p = NumericPolicy.exact()
-    table: Dict[str, Dict[int, Dict[str, float]]] = {p.name: {} for p in policies}
-    rows = []
+    P, L = len(policies), len(lengths)
+    vals = torch.empty((P + 1, L, seeds), dtype=torch.float64, device=dev)  # [0]: exact
+    clamps = torch.zeros((P, L, seeds), dtype=torch.int64, device=dev)
     scal = torch.zeros(2, dtype=torch.float64, device=dev)
-    for n in lengths:
-        ab = []
-        for seed in range(seeds):
-            rs = np.random.default_rng(seed * 7919 + n)
-            ab.append((heavy_tailed(rs, n, sigma), heavy_tailed(rs, n, sigma)))
-        A = torch.from_numpy(np.stack([a for a, _ in ab])).to(dev)
-        B = torch.from_numpy(np.stack([b for _, b in ab])).to(dev)
+    kept = {}
+    for li, n in enumerate(lengths):
+        if host_inputs:
+            ab = []
+            for seed in range(seeds):
+                rs = np.random.default_rng(seed * 7919 + n)
+                ab.append((heavy_tailed(rs, n, sigma), heavy_tailed(rs, n, sigma)))
+            A = torch.from_numpy(np.stack([a for a, _ in ab])).to(dev)
+            B = torch.from_numpy(np.stack([b for _, b in ab])).to(dev)
+        else:
+            A, B = dot_sweep_inputs_dev(n, seeds, sigma, device)
+        if keep_inputs:
+            kept[n] = (A, B)
         op = contraction(batch=seeds, rows=1, cols=1, depth=n, a_batch=n, a_row=0, a_k=1,
                          b_batch=n, b_col=0, b_k=1, c_batch=1, c_row=1)
-        exact = torch.empty(seeds, dtype=torch.float64, device=dev)
-        contract_dev(exact_p, op, A, B, exact)
-        ex = exact.cpu().numpy()
-        for p in policies:
+        contract_dev(exact_p, op, A, B, vals[0, li])
+        qa, qb = torch.empty_like(A), torch.empty_like(B)
+        for pi, p in enumerate(policies):
             f = p.input_format
-            qa, qb = A, B
-            cl = torch.zeros(seeds, dtype=torch.int64, device=dev)
-            rowwise = (f is not None and p.input_rounding != Rounding.STOCHASTIC
-                       and p.scaling != Scaling.MX_BLOCK)
-            if rowwise:  # every vector its own tensor, one launch per operand
-                qa, qb = torch.empty_like(A), torch.empty_like(B)
+            cl = clamps[pi, li]
+            a, b = A, B
+            if f is not None and p.input_rounding != Rounding.STOCHASTIC \
+                    and p.scaling != Scaling.MX_BLOCK:
+                # Every vector its own tensor: one launch per operand.
                 quantize_rows_dev(p, f, p.input_rounding, A, qa, d_clamped=cl)
                 quantize_rows_dev(p, f, p.input_rounding, B, qb, d_clamped=cl)
+                a, b = qa, qb
             elif f is not None:
-                qa, qb = torch.empty_like(A), torch.empty_like(B)
                 for seed in range(seeds):
                     st = torch.tensor([0xD1F7 + seed], dtype=torch.int64, device=dev)
                     for src, dst in ((A[seed], qa[seed]), (B[seed], qb[seed])):
-                        amax_dev(src, scal[0:1])
-                        per_tensor_scale_dev(f, scal[0:1], scal[1:2])
-                        quantize_dev(p, f, p.input_rounding, src, dst, d_scale=scal[1:2],
+                        sc = None
+                        if p.scaling == Scaling.PER_TENSOR:
+                            amax_dev(src, scal[0:1])
+                            per_tensor_scale_dev(f, scal[0:1], scal[1:2])
+                            sc = scal[1:2]
+                        quantize_dev(p, f, p.input_rounding, src, dst, d_scale=sc,
                                      d_rng_state=st, d_clamped=cl[seed:seed + 1])
-            got = torch.empty(seeds, dtype=torch.float64, device=dev)
-            contract_dev(p, op, qa, qb, got)
-            check_dev()
-            v, c = got.cpu().numpy(), cl.cpu().numpy()
-            errs = np.abs(v - ex) / np.abs(ex)
+                a, b = qa, qb
+            contract_dev(p, op, a, b, vals[pi + 1, li])
+    med = torch.empty((P, L), dtype=torch.float64, device=dev)
+    exact_rep = vals[0:1].expand(P, L, seeds).contiguous()
+    group_kth_rel_error_dev(vals[1:], exact_rep, P * L, seeds, seeds // 2, med)
+    check_dev()
+    v, c, m = vals.cpu().numpy(), clamps.cpu().numpy(), med.cpu().numpy()
+    table: Dict[str, Dict[int, Dict[str, float]]] = {p.name: {} for p in policies}
+    rows = []
+    for pi, p in enumerate(policies):
+        for li, n in enumerate(lengths):
+            table[p.name][n] = {"median_rel_error": float(m[pi, li]),
+                                "clamped_per_pair": float(c[pi, li].sum()) / seeds}
             for seed in range(seeds):
-                rows.append((p.name, n, seed, float(v[seed]), float(ex[seed]), int(c[seed])))
-            e = np.sort(errs)
-            table[p.name][n] = {"median_rel_error": float(e[len(e) // 2]),
-                                "clamped_per_pair": float(c.sum()) / seeds}
-    return {"table": table, "rows": rows}
+                rows.append((p.name, n, seed, float(v[pi + 1, li, seed]), float(v[0, li, seed]),
+                             int(c[pi, li, seed])))
+    out = {"table": table, "rows": rows}
+    if keep_inputs:
+        out["inputs"] = {n: (a.cpu().numpy(), b.cpu().numpy()) for n, (a, b) in kept.items()}
+    return out
 
 
 def real_dot_policies() -> List[NumericPolicy]:
@@ -248,6 +289,62 @@ def real_dot_batch(X=None, W=None, policies=None) -> Dict[str, Dict[str, float]]
     return out
 
 
+def real_dot_batch_dev(X=None, W=None, policies=None, device: int = 0) -> Dict:
+    """real_dot_batch on the device: X and W cross to the GPU once; per policy
+    the whole-tensor per-tensor scales, the casts of X then W on the policy's
+    Rng(7) (RealDotSweep.java:235-254), the contraction, the true median of
+    the relative errors (two radix selections) and the RMS sums, all on the
+    device; one read-back at the end. The medians are exact order statistics
+    of bit-exact outputs; the RMS ratio comes from a parallel sum, so it
+    agrees with the sequential Java sum to rounding."""
+    import torch
+
+    from .kernel import (amax_dev, check_dev, error_sums_dev, gemm_dev, per_tensor_scale_dev,
+                         quantize_dev)
+    from .stats import RADIX_BINS, select_rel_error_dev
+
+    if X is None:
+        X, W = real_dot_inputs()
+    policies = policies or real_dot_policies()
+    dev = torch.device("cuda", device)
+    Xd = torch.from_numpy(np.ascontiguousarray(X)).to(dev)
+    Wd = torch.from_numpy(np.ascontiguousarray(W)).to(dev)
+    M, K = Xd.shape
+    N = Wd.shape[0]
+    total = M * N
+    exact = torch.empty((M, N), dtype=torch.float64, device=dev)
+    gemm_dev(NumericPolicy.exact(), Xd, Wd, exact)
+    C = torch.empty_like(exact)
+    qx, qw = torch.empty_like(Xd), torch.empty_like(Wd)
+    scal = torch.zeros(2, dtype=torch.float64, device=dev)
+    P = len(policies)
+    sums = torch.zeros((P, 2), dtype=torch.float64, device=dev)
+    med = torch.zeros((P, 2, 2), dtype=torch.int64, device=dev)
+    hist = torch.empty(RADIX_BINS, dtype=torch.int64, device=dev)
+    for k, p in enumerate(policies):
+        f = p.input_format
+        st = torch.tensor([7], dtype=torch.int64, device=dev)
+        a, b = Xd, Wd
+        if f is not None:
+            for src, dst in ((Xd, qx), (Wd, qw)):
+                amax_dev(src, scal[0:1])
+                per_tensor_scale_dev(f, scal[0:1], scal[1:2])
+                quantize_dev(p, f, p.input_rounding, src, dst, d_scale=scal[1:2], d_rng_state=st)
+            a, b = qx, qw
+        gemm_dev(p, a, b, C, d_rng_state=st)
+        error_sums_dev(C, exact, sums[k])
+        select_rel_error_dev(C, exact, total // 2 - 1, med[k, 0], hist)
+        select_rel_error_dev(C, exact, total // 2, med[k, 1], hist)
+    check_dev()
+    s, m = sums.cpu().numpy(), med[:, :, 0].cpu().numpy()
+    out = {}
+    for k, p in enumerate(policies):
+        lo, hi = (float(np.int64(x).view(np.float64)) for x in m[k])
+        out[p.name] = {"median_rel_error": 0.5 * (lo + hi),
+                       "rms_error_ratio": float(np.sqrt(s[k, 0] / s[k, 1]))}
+    return out
+
+
 def mx_policies() -> List[NumericPolicy]:
     """The block-scaled study: e4m3 and e2m1 under per-tensor, MX spec and MX +1
     scaling, FP32 sequential accumulation (DotSweep.java:71-82's scaling group)."""
@@ -260,16 +357,10 @@ def mx_policies() -> List[NumericPolicy]:
     return ps
 
 
-def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0) -> Dict:
-    """The block-scaled GEMM at size^3 on device-resident tensors. Per policy:
-    median relative error (upper), RMS ratio, clamps per vector pair (clamps in
-    row i of A plus row j of W, averaged over pairs, as DotSweep.java:119-120
-    counts them) and per pair of 32-blocks."""
+def mx_gemm_inputs(size: int = 4096, seed: int = 0, device: int = 0):
+    """The block-scaled study's operands: A and W of size x size, fp32
+    N(0,1) x lognormal(0,1) values held as doubles, the same on every rank."""
     import torch
-
-    from .kernel import (amax_dev, check_dev, error_sums_dev, gemm_dev, per_tensor_scale_dev,
-                         quantize_dev)
-    from .stats import upper_median_rel_error
 
     dev = torch.device("cuda", device)
     g = torch.Generator(device=dev)
@@ -278,32 +369,68 @@ def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0) -> 
          torch.exp(torch.randn(size, size, device=dev, generator=g))).double()
     W = (torch.randn(size, size, device=dev, generator=g) *
          torch.exp(torch.randn(size, size, device=dev, generator=g))).double()
-    exact = torch.empty_like(A)
-    gemm_dev(NumericPolicy.exact(), A, W, exact)
-    qa, qw, C = torch.empty_like(A), torch.empty_like(W), torch.empty_like(A)
+    return A, W
+
+
+def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0, dist=None,
+            inputs=None) -> Dict:
+    """The block-scaled GEMM at size^3 on device-resident tensors. Per policy:
+    median relative error (upper), RMS ratio, clamps per vector pair (clamps in
+    row i of A plus row j of W, averaged over pairs, as DotSweep.java:119-120
+    counts them) and per pair of 32-blocks.
+
+    With a process group `dist`, the GEMMs are sharded by N-tile
+    (drift_b200.dist.ntile_gemm): every rank casts all of A and its block of
+    W's rows (a per-tensor scale of W from the all-reduced amax), contracts
+    its block of C's columns, and only statistics cross ranks (error sums and
+    W's clamp counts summed, the median's radix histograms all-reduced). The
+    results are those of one GPU."""
+    import torch
+
+    from . import dist as ddist
+    from .kernel import (amax_dev, check_dev, error_sums_dev, gemm_dev, per_tensor_scale_dev,
+                         quantize_dev)
+    from .stats import upper_median_rel_error
+
+    world = dist.get_world_size() if dist is not None else 1
+    rank = dist.get_rank() if dist is not None else 0
+    A, W = inputs if inputs is not None else mx_gemm_inputs(size, seed, device)
+    dev = A.device
+    lo, hi = ddist.ntile_bounds(size, world, rank)
+    Wc = W[lo:hi]
+    exact = torch.empty((size, hi - lo), dtype=torch.float64, device=dev)
+    ddist.ntile_gemm(NumericPolicy.exact(), A, Wc, exact)
+    qa, qw = torch.empty_like(A), torch.empty_like(Wc)
+    C = torch.empty_like(exact)
     scal = torch.zeros(4, dtype=torch.float64, device=dev)
     res = {}
     for p in (policies or mx_policies()):
         f = p.input_format
         cl = torch.zeros(2, dtype=torch.int64, device=dev)
-        for k, (src, dst) in enumerate(((A, qa), (W, qw))):
-            if p.scaling == Scaling.PER_TENSOR:
-                amax_dev(src, scal[k:k + 1])
-                per_tensor_scale_dev(f, scal[k:k + 1], scal[2 + k:3 + k])
-                quantize_dev(p, f, Rounding.NEAREST_EVEN, src, dst, d_scale=scal[2 + k:3 + k],
-                             d_clamped=cl[k:k + 1])
-            else:
-                quantize_dev(p, f, Rounding.NEAREST_EVEN, src, dst, d_clamped=cl[k:k + 1])
-        gemm_dev(p, qa, qw, C)
+        if p.scaling == Scaling.PER_TENSOR:
+            amax_dev(A, scal[0:1])
+            per_tensor_scale_dev(f, scal[0:1], scal[2:3])
+            quantize_dev(p, f, Rounding.NEAREST_EVEN, A, qa, d_scale=scal[2:3], d_clamped=cl[0:1])
+            ddist.sharded_scale(f, Wc, scal[1:2], scal[3:4], dist)
+            quantize_dev(p, f, Rounding.NEAREST_EVEN, Wc, qw, d_scale=scal[3:4],
+                         d_clamped=cl[1:2])
+        else:
+            quantize_dev(p, f, Rounding.NEAREST_EVEN, A, qa, d_clamped=cl[0:1])
+            quantize_dev(p, f, Rounding.NEAREST_EVEN, Wc, qw, d_clamped=cl[1:2])
+        ddist.ntile_gemm(p, qa, qw, C)
         check_dev()
         # Statistics on the engine's own kernels: the upper median by radix
         # selection, the RMS ratio from two device sums.
         sums = torch.zeros(2, dtype=torch.float64, device=dev)
         error_sums_dev(C, exact, sums)
+        wcl = cl[1:2].clone()
+        if dist is not None:
+            dist.all_reduce(sums)
+            dist.all_reduce(wcl)
         err_sq, ex_sq = (float(x) for x in sums.cpu())
-        ca, cw = (int(x) for x in cl.cpu())
+        ca, cw = int(cl[0].item()), int(wcl.item())
         per_pair = ca / size + cw / size
-        res[p.name] = {"median_rel_error": upper_median_rel_error(C, exact, C.numel()),
+        res[p.name] = {"median_rel_error": upper_median_rel_error(C, exact, size * size, dist),
                        "rms_error_ratio": float(np.sqrt(err_sq / ex_sq)),
                        "clamped_per_pair": per_pair,
                        "clamped_per_block_pair": per_pair / (size // 32)}

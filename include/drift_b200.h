@@ -380,6 +380,20 @@ DRIFT_API int drift_radix_select_dev(drift_ctx *ctx, int pass,
                                      const uint64_t *d_hist, uint64_t *d_state,
                                      void *stream);
 
+/*
+ * The same order statistic within each of `groups` groups of n outputs
+ * (group g holds d_got[g*n .. g*n+n) and the same span of d_exact): writes
+ * the k-th smallest relative error of group g (0 <= k < n) to d_out[g], NaN
+ * sorting after +Inf. One launch for many small groups, such as the
+ * per-(policy, length) medians over DotSweep's seeds
+ * (java/.../tools/DotSweep.java:152-153). n <= DRIFT_GROUP_MAX.
+ */
+#define DRIFT_GROUP_MAX 4096
+DRIFT_API int drift_group_kth_rel_error_dev(drift_ctx *ctx, const double *d_got,
+                                            const double *d_exact, int64_t groups,
+                                            int64_t n, int64_t k, double *d_out,
+                                            void *stream);
+
 /* ----------------------------------------------------------- diagnostics */
 /*
  * A batched contraction with per-row windows: the attention matmuls of

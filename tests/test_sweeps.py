@@ -67,6 +67,14 @@ def test_real_shape_batch_every_output():
         assert clamped == cl
     stats = sweeps.real_dot_batch(X, W)
     assert stats["fp32 sequential"]["median_rel_error"] < stats["bf16 sequential"]["median_rel_error"]
+    # The device-resident driver: the same true medians bit for bit (order
+    # statistics of the same bit-exact outputs), RMS ratios to rounding.
+    dev = sweeps.real_dot_batch_dev(X, W)
+    assert dev.keys() == stats.keys()
+    for name in stats:
+        assert dev[name]["median_rel_error"] == stats[name]["median_rel_error"], name
+        assert dev[name]["rms_error_ratio"] == pytest.approx(stats[name]["rms_error_ratio"],
+                                                             rel=1e-12), name
 
 
 def test_mx_gemm_sampled_outputs():
@@ -121,7 +129,7 @@ def test_device_dot_sweep_equals_host_sweep():
     from drift_b200 import sweeps
 
     host = sweeps.dot_sweep(lengths=(16, 100, 1024), seeds=7)
-    dev = sweeps.dot_sweep_dev(lengths=(16, 100, 1024), seeds=7)
+    dev = sweeps.dot_sweep_dev(lengths=(16, 100, 1024), seeds=7, host_inputs=True)
     key = lambda r: (r[0], r[1], r[2])
     h, g = sorted(host["rows"], key=key), sorted(dev["rows"], key=key)
     assert len(h) == len(g)
@@ -130,3 +138,26 @@ def test_device_dot_sweep_equals_host_sweep():
         assert np.float64(a[3]).view(np.int64) == np.float64(b[3]).view(np.int64), a[:3]
         assert np.float64(a[4]).view(np.int64) == np.float64(b[4]).view(np.int64), a[:3]
     assert host["table"] == dev["table"]
+
+
+def test_device_dot_sweep_full_shape_against_oracle():
+    """The dot sweep at its configuration (200 seeds x lengths 16..4096, 10
+    policies) with inputs generated on the device: every dot and clamp count
+    against the oracle on the same vectors (read back for the check), and the
+    device medians against the upper median of the rows."""
+    from drift_b200 import sweeps
+
+    lengths = tuple(2 ** k for k in range(4, 13))
+    out = sweeps.dot_sweep_dev(lengths=lengths, seeds=200, keep_inputs=True)
+    pols = {p.name: p for p in sweeps.dot_sweep_policies()}
+    errs = {}
+    for name, n, seed, value, exact, clamped in out["rows"]:
+        a, b = out["inputs"][n][0][seed], out["inputs"][n][1][seed]
+        v, c = _oracle_dot_run(pols[name], a, b, seed)
+        assert np.float64(v).view(np.int64) == np.float64(value).view(np.int64), (name, n, seed)
+        assert c == clamped, (name, n, seed)
+        ex, _ = O.dot(a, 0, 1, b, 0, 1, n, _op(sweeps.NumericPolicy.exact()))
+        assert ex == exact
+        errs.setdefault((name, n), []).append(abs(value - exact) / abs(exact))
+    for (name, n), e in errs.items():
+        assert out["table"][name][n]["median_rel_error"] == sorted(e)[len(e) // 2], (name, n)
