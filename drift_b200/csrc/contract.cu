@@ -78,9 +78,32 @@ __device__ __forceinline__ void window_of(const ContractArgs &g, int64_t i, int6
 // (idx + cnt)-th number of the stream only when the fraction is non-zero.
 // `z` is the splitmix64 counter of the next draw, state + (idx + cnt + 1) *
 // golden; a dot's draws are consecutive, so it advances by golden per draw.
+//
+// A sum in the accumulator's normal range below its top binade (every sum of
+// ordinary data) is rounded on its bit pattern with integer operations only:
+// its S = 52 - mant low significand bits are the fraction, scaled by 2^S;
+// Java draws when they are non-zero, rounds up when nextDouble() < frac,
+// that is when (mix >> 11) * 2^-53 < dropped * 2^-S, which for integers is
+// (mix >> (64 - S)) < dropped; and rounding up adds 1 at bit S (a carry into
+// the exponent is the next binade's value). No saturation can occur below the
+// top binade. The other sums take the general form below.
 template <int ACC>
 __device__ __forceinline__ double sr_round(double x, uint64_t &z, uint32_t &cnt) {
     using F = AccFmt<ACC>;
+    constexpr int S = 52 - F::mant;
+    const uint64_t bits = (uint64_t)__double_as_longlong(x);
+    const unsigned ex = (unsigned)(bits >> 52) & 0x7FFu;
+    if (ex - (unsigned)(1023 + F::min_exp) <= (unsigned)(F::max_exp - 1 - F::min_exp)) {
+        const uint64_t dropped = bits & ((1ULL << S) - 1);
+        uint64_t r = bits - dropped;
+        if (dropped != 0) {
+            const uint64_t mix = splitmix_mix(z);
+            z += kGolden;
+            cnt++;
+            if ((mix >> (64 - S)) < dropped) r += 1ULL << S;
+        }
+        return __longlong_as_double((long long)r);
+    }
     if (x == 0.0 || isnan(x)) return x;
     const double ax = fabs(x);
     if (isinf(ax)) return copysign(F::max(), x);

@@ -148,3 +148,55 @@ def test_value_domain_cast_matches_oracle(fmt):
                                   O.STOCHASTIC, x, 1.0, 0x5EED)
     assert st == want_st
     assert (got.view(np.int64) == want.view(np.int64)).all()
+
+
+# ------------------------------------------------------------------ stochastic accumulator
+
+def _sr_round_bits(x, acc, state):
+    """Dot.round(x, acc, STOCHASTIC, rng) on x's bit pattern, the form the
+    stochastic-accumulator kernels use for sums in the accumulator's normal
+    range below its top binade: with S dropped significand bits, the draw is
+    taken only when those bits are non-zero, nextDouble() < frac is
+    (mix >>> (64 - S)) < dropped, and rounding up adds 1 at bit S. Returns
+    (value or None when the sum needs the general form, new state)."""
+    import ctypes
+
+    mant, min_e, max_e = (10, -14, 15) if acc == O.ACC_FP16 else (7, -126, 127)
+    S = 52 - mant
+    bits = int(np.float64(x).view(np.uint64))
+    E = (bits >> 52) & 0x7FF
+    if not (1023 + min_e <= E <= 1023 + max_e - 1):
+        return None, state
+    dropped = bits & ((1 << S) - 1)
+    r = bits - dropped
+    if dropped:
+        st = ctypes.c_uint64(state)
+        mix = O.lib().o_rng_next_long(ctypes.byref(st))
+        state = st.value
+        if (mix >> (64 - S)) < dropped:
+            r += 1 << S
+    return float(np.uint64(r).view(np.float64)), state
+
+
+@pytest.mark.parametrize("acc", [O.ACC_FP16, O.ACC_BF16])
+def test_bit_pattern_stochastic_rounding_matches_oracle(acc):
+    rs = np.random.default_rng(31 + acc)
+    n = 20_000
+    mant, min_e, max_e = (10, -14, 15) if acc == O.ACC_FP16 else (7, -126, 127)
+    x = np.ldexp(rs.random(n) + 1.0, rs.integers(min_e - 3, max_e + 2, n))
+    x *= np.where(rs.random(n) < 0.5, -1.0, 1.0)
+    # Values with no dropped bits (no draw) and with a single low bit set.
+    x[::7] = np.ldexp(rs.integers(1 << mant, 1 << (mant + 1), x[::7].size), -mant)
+    x[3::11] = np.nextafter(x[3::11], np.inf)
+    state, taken = 0xC0FFEE, 0
+    for v in x:
+        got, s2 = _sr_round_bits(v, acc, state)
+        want, w2 = O.acc_round(acc, O.STOCHASTIC, np.array([v]), state)
+        if got is None:        # the general form's range: skip, keep the streams aligned
+            state = w2
+            continue
+        taken += 1
+        assert np.float64(got).view(np.int64) == want.view(np.int64)[0], v
+        assert s2 == w2, v
+        state = s2
+    assert taken > n // 2
