@@ -104,21 +104,28 @@ def dot_sweep(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)), seed
     return {"table": table, "rows": rows}
 
 
-def dot_sweep_inputs_dev(n: int, seeds: int, sigma: float = 1.0, device: int = 0):
-    """The dot sweep's vectors of length n for every seed, generated on the
-    device: two seeds x n tensors of fp32 N(0,1) x lognormal(0, sigma) values
-    held as doubles (row s is seed s's vector), seeded by n."""
+def dot_sweep_inputs_dev(lengths: Sequence[int], seeds: int, sigma: float = 1.0,
+                         device: int = 0) -> Dict[int, tuple]:
+    """The dot sweep's vectors for every length and seed, generated on the
+    device in one seeded draw per operand: for each n, two seeds x n tensors
+    of fp32 N(0,1) x lognormal(0, sigma) values held as doubles (row s is
+    seed s's vector), each a contiguous block of one buffer."""
     import torch
 
     dev = torch.device("cuda", device)
     g = torch.Generator(device=dev)
-    g.manual_seed(7919 + n)
+    g.manual_seed(7919)
+    total = seeds * sum(lengths)
     out = []
     for _ in range(2):
-        x = torch.randn(seeds, n, device=dev, generator=g)
-        x *= torch.exp(torch.randn(seeds, n, device=dev, generator=g) * sigma)
+        x = torch.randn(total, device=dev, generator=g)
+        x *= torch.exp(torch.randn(total, device=dev, generator=g) * sigma)
         out.append(x.double())
-    return out[0], out[1]
+    blocks, off = {}, 0
+    for n in lengths:
+        blocks[n] = tuple(t[off:off + seeds * n].view(seeds, n) for t in out)
+        off += seeds * n
+    return blocks
 
 
 def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
@@ -150,6 +157,7 @@ def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
     clamps = torch.zeros((P, L, seeds), dtype=torch.int64, device=dev)
     scal = torch.zeros(2, dtype=torch.float64, device=dev)
     kept = {}
+    generated = None if host_inputs else dot_sweep_inputs_dev(lengths, seeds, sigma, device)
     for li, n in enumerate(lengths):
         if host_inputs:
             ab = []
@@ -159,7 +167,7 @@ def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
             A = torch.from_numpy(np.stack([a for a, _ in ab])).to(dev)
             B = torch.from_numpy(np.stack([b for _, b in ab])).to(dev)
         else:
-            A, B = dot_sweep_inputs_dev(n, seeds, sigma, device)
+            A, B = generated[n]
         if keep_inputs:
             kept[n] = (A, B)
         op = contraction(batch=seeds, rows=1, cols=1, depth=n, a_batch=n, a_row=0, a_k=1,
@@ -193,16 +201,15 @@ def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
     exact_rep = vals[0:1].expand(P, L, seeds).contiguous()
     group_kth_rel_error_dev(vals[1:], exact_rep, P * L, seeds, seeds // 2, med)
     check_dev()
-    v, c, m = vals.cpu().numpy(), clamps.cpu().numpy(), med.cpu().numpy()
+    v, c, m = vals.cpu().tolist(), clamps.cpu().tolist(), med.cpu().tolist()
     table: Dict[str, Dict[int, Dict[str, float]]] = {p.name: {} for p in policies}
-    rows = []
     for pi, p in enumerate(policies):
         for li, n in enumerate(lengths):
-            table[p.name][n] = {"median_rel_error": float(m[pi, li]),
-                                "clamped_per_pair": float(c[pi, li].sum()) / seeds}
-            for seed in range(seeds):
-                rows.append((p.name, n, seed, float(v[pi + 1, li, seed]), float(v[0, li, seed]),
-                             int(c[pi, li, seed])))
+            table[p.name][n] = {"median_rel_error": m[pi][li],
+                                "clamped_per_pair": float(sum(c[pi][li])) / seeds}
+    rows = [(p.name, n, seed, v[pi + 1][li][seed], v[0][li][seed], c[pi][li][seed])
+            for pi, p in enumerate(policies) for li, n in enumerate(lengths)
+            for seed in range(seeds)]
     out = {"table": table, "rows": rows}
     if keep_inputs:
         out["inputs"] = {n: (a.cpu().numpy(), b.cpu().numpy()) for n, (a, b) in kept.items()}
