@@ -849,8 +849,14 @@ int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
         return DRIFT_EINVAL;
     ContractArgs g = args_of(p, d);
     const unsigned grid = grid_of(total);
+    // Problems of fewer outputs than one staged CTA (a batch of single dots,
+    // as the dot sweep runs them) go to the one-output-per-thread kernel: on
+    // the tiled or staged kernels each such problem held a whole CTA that
+    // walked all of K for a handful of live outputs (the dot sweep's 200-dot
+    // batches ran 20x slower there).
+    const bool tiny = d.op.rows * d.op.cols < (int64_t)kStageSide * kStageSide;
 
-    if (!stochastic(p) && tiled_route(d)) {
+    if (!stochastic(p) && !tiny && tiled_route(d)) {
         const drift_contraction &op = d.op;
         rc = launch_gemm_batched(ws, cache, p, op.batch, op.rows, op.cols, op.depth, g.A, op.a_row,
                                  op.a_k, op.a_batch, g.B, op.b_col, op.b_k, op.b_batch, nullptr,
@@ -863,7 +869,8 @@ int launch_contract(Workspace &ws, ScheduleCache &cache, const drift_policy *p,
     // staged kernel walks chunk by chunk: one output per thread with the
     // operands staged per 16 x 16 tile. Pairwise (a tree per row) and blocked
     // chunks off the chunk edges stay on the per-thread kernel below.
-    if (!stochastic(p) && staged_walk(p->order, g.acc_block, d.op.window) && staged_fits(d.op))
+    if (!stochastic(p) && !tiny && staged_walk(p->order, g.acc_block, d.op.window) &&
+        staged_fits(d.op))
         return launch_contract_staged(p, d, nullptr, nullptr, st);
     if (!stochastic(p)) {
         const bool tr = p->acc_rounding == DRIFT_TRUNCATE;
