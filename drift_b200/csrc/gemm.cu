@@ -69,9 +69,10 @@ constexpr int GEMM_SMEM = STAGES * STAGE_DOUBLES * (int)sizeof(double) + 64;
 // Pairwise leaves over a full tile are validated once per tile (mac16_run,
 // one check, the two leaves redone exactly from zero on a miss) for the FP32
 // and BF16 accumulators. Measured at 8192^3 on one B200: FP32 pairwise +8%.
-// Not for FP16, whose normal range starts at 2^-14: a leaf starts from one
-// product, and small products fall below it often enough that a large share
-// of tiles would be redone (2.5x slower); nor for the sequential and blocked
+// Not for FP16, whose normal range starts at 2^-14: on N(0,1) x lognormal
+// data about 0.1% of products fall below it, so a thread's tile misses about
+// 3.7% of the time, and a warp redoes the tile when any of its 32 lanes
+// misses, 70% of warp-tiles (2.5x slower). Nor for the sequential and blocked
 // orders, which lost 4-5% with a tile-start copy of the accumulators in
 // shared memory to restart from.
 template <int ACC, int ORDER>
