@@ -4,7 +4,7 @@
 Workload (the reference's large policy sweep): GEMMs of M = N = K = 8192 on
 N(0,1) x lognormal(0,1) inputs held as fp32 values in doubles; the 12
 accumulator x order x cast policies of RealDotSweep
-(java/src/main/java/io/drift/tools/RealDotSweep.java:212-223) plus the FP64
+(java/src/main/java/io/drift/tools/RealDotSweep.java:97-108) plus the FP64
 exact GEMM they are scored against. One step on one rank is one seed: cast,
 contract and score all 12 policies and run the exact GEMM. Each rank takes its
 own seed (rank + world * step), so per-GPU work is fixed as GPUs are added
@@ -16,8 +16,9 @@ statistics are summed across ranks with NCCL all-reduce.
 
 `value` counts every emulated multiply-accumulate (13 GEMMs per step per
 rank) over the max-over-ranks device time of the K timed steps. `e2e` runs the
-same steps through the C ABI with pinned host buffers (every input copied in
-and every output copied out inside the timed region).
+same step through the C ABI's one-call sweep (drift_real_dot_sweep) on pinned
+host buffers: both operands copied in and the statistics read back inside the
+timed region, every step.
 """
 from __future__ import annotations
 
@@ -51,7 +52,7 @@ SWEEP_NAMES = ["fp32 sequential", "fp32 pairwise", "fp32 blocked", "fp16 sequent
 
 
 def sweep_policies(d):
-    """RealDotSweep's policy list (RealDotSweep.java:212-223)."""
+    """RealDotSweep's policy list (RealDotSweep.java:97-108)."""
     from drift_b200 import sweeps
 
     return sweeps.policy_sweep_policies()
@@ -445,57 +446,51 @@ def run_engine(args):
 
 
 def run_e2e(d, args, A, B, pols, exact_p, world, rank, pg):
-    """The same steps through the reference-facing host entry points
-    (drift_quantize / drift_gemm on pinned host buffers)."""
-    import numpy as np
+    """The same step through the reference-facing host entry point: one
+    drift_real_dot_sweep call per step on pinned host copies of this rank's
+    A and B (RealDotSweep's loop, RealDotSweep.java:119-142). Inside the timed
+    region, every step copies both operands in, runs the exact GEMM and the 12
+    policies' casts, contractions and statistics, and reads the statistics
+    back; only statistics cross back, as in the reference, which keeps the
+    outputs in the loop that scores them."""
     import torch
+
+    from drift_b200 import dist as ddist
+    from drift_b200 import sweeps
 
     S = args.size
     hA = torch.empty((S, S), dtype=torch.float64, pin_memory=True)
     hB = torch.empty((S, S), dtype=torch.float64, pin_memory=True)
     hA.copy_(A)
     hB.copy_(B)
-    hqA = torch.empty_like(hA, pin_memory=True)
-    hqB = torch.empty_like(hB, pin_memory=True)
-    hC = torch.empty_like(hA, pin_memory=True)
-    a, b, qa, qb, cc = (x.numpy() for x in (hA, hB, hqA, hqB, hC))
-    h2d = d2h = 0
+    a, b = hA.numpy(), hB.numpy()
+    P = len(pols)
+    # Per step: both operands and the radix selections' start states in; the
+    # sums, clamp counts, selected medians and the error word out.
+    h2d = a.nbytes + b.nbytes + 4 * 8 * P
+    d2h = (2 + 2 + 4) * 8 * P + 4
 
     def one_step():
-        nonlocal h2d, d2h
-        h2d = d2h = 0
-        d.gemm(exact_p, S, S, S, a, 0, S, 1, b, 0, S, 1, out=cc)
-        h2d += 2 * a.nbytes
-        d2h += cc.nbytes
-        for p in pols:
-            x, y = a, b
-            f = p.input_format
-            if f is not None:
-                sa = d.Quant.per_tensor_scale(f, d.Quant.amax(a)) if p.scaling == 1 else 1.0
-                sb = d.Quant.per_tensor_scale(f, d.Quant.amax(b)) if p.scaling == 1 else 1.0
-                d.Quant.quantize(a, 0, qa, 0, a.size, f, p, sa, None)
-                d.Quant.quantize(b, 0, qb, 0, b.size, f, p, sb, None)
-                h2d += 2 * a.nbytes + (2 * a.nbytes if p.scaling == 1 else 0)
-                d2h += 2 * a.nbytes
-                x, y = qa, qb
-            d.gemm(p, S, S, S, x, 0, S, 1, y, 0, S, 1, out=cc)
-            h2d += 2 * a.nbytes
-            d2h += cc.nbytes
+        return sweeps.real_dot_sweep(a, b, pols)
 
     one_step()  # warm-up
     steps = max(1, args.e2e_steps)
     if pg is not None:
         pg.barrier()
+    torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(steps):
-        one_step()
+        out = one_step()
     dt = time.perf_counter() - t0
-    from drift_b200 import dist as ddist
-
     dt = ddist.max_over_ranks(dt, pg, torch.device("cuda", torch.cuda.current_device()))
-    macs = (len(pols) + 1) * S ** 3 * world * steps
+    macs = (P + 1) * S ** 3 * world * steps
     return {"value": macs / dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": steps, "path": "drift_quantize/drift_amax/drift_gemm on pinned host buffers"}
+            "steps": steps,
+            "path": "drift_real_dot_sweep on pinned host buffers (one C-ABI call per step; "
+                    "statistics per rank)",
+            "stats_rank0": {k: {"median_rel_error": v["median_rel_error"],
+                                "rms_error_ratio": v["rms_error_ratio"]}
+                            for k, v in out.items()} if rank == 0 else None}
 
 
 # ------------------------------------------------------------------ reference arm

@@ -97,6 +97,8 @@ SIGNATURES = {
     "drift_radix_hist_dev": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp]),
     "drift_radix_select_dev": (_int, [_vp, _int, _vp, _vp, _vp]),
     "drift_group_kth_rel_error_dev": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
+    "drift_real_dot_sweep": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _vp, _vp, ctypes.c_uint64,
+                                    _vp]),
     "drift_embed_gather_dev": (_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "drift_embed_grad_dev": (_int, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp]),
     "drift_bias_grad_dev": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),

@@ -692,6 +692,122 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
     return DRIFT_OK;
 }
 
+// ------------------------------------------------------------------ RealDotSweep in one call
+//
+// RealDotSweep's per-policy loop (RealDotSweep.java:119-142) over one pair of
+// host tensors: X and W cross once, and everything else stays on the device
+// until the statistics come back. Per policy, in Java's order: a fresh Rng,
+// the whole-tensor per-tensor scales, X's cast then W's, the contraction,
+// then the true median of the relative errors (two radix selections) and the
+// RMS sums against the exact FP64 contraction.
+int drift_real_dot_sweep(drift_ctx *ctx, const drift_policy *policies, int n_policies,
+                         int64_t M, int64_t N, int64_t K, const double *X, const double *W,
+                         uint64_t rng_seed, double *stats_out) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!policies || n_policies < 0 || M <= 0 || N <= 0 || K <= 0 || !X || !W ||
+        (n_policies > 0 && !stats_out))
+        return fail(DRIFT_EINVAL, "bad arguments");
+    if (n_policies == 0) return DRIFT_OK;
+    cudaStream_t st = ctx->stream;
+    const int64_t nx = M * K, nw = N * K, nc = M * N, P = n_policies;
+    // Device layout: X, W, their casts, C, the exact C, then per policy two
+    // sums, two clamp counts, two radix states of two words, and scratch.
+    const size_t words = (size_t)(2 * nx + 2 * nw + 2 * nc) + (size_t)P * 8 + DRIFT_RADIX_BINS + 8;
+    double *d_x = (double *)ctx->io.get(words * 8 + 512, st);
+    if (!d_x) return fail(DRIFT_ENOMEM, "staging");
+    double *d_w = d_x + nx, *d_qx = d_w + nw, *d_qw = d_qx + nx, *d_c = d_qw + nw;
+    double *d_exact = d_c + nc;
+    double *d_sums = d_exact + nc;                                          // P x 2
+    unsigned long long *d_cl = (unsigned long long *)(d_sums + 2 * P);     // P x 2
+    unsigned long long *d_med = d_cl + 2 * P;                              // P x 2 x 2
+    unsigned long long *d_hist = d_med + 4 * P;                            // radix bins
+    double *d_scal = (double *)(d_hist + DRIFT_RADIX_BINS);                  // amax, scale
+    uint64_t *d_state = (uint64_t *)(d_scal + 4);
+    // Radix states start at (0, k) for k = total/2 - 1 and total/2.
+    std::vector<unsigned long long> med0((size_t)P * 4);
+    for (int64_t p = 0; p < P; p++) {
+        med0[4 * p + 0] = 0;
+        med0[4 * p + 1] = (unsigned long long)(nc / 2 - 1);
+        med0[4 * p + 2] = 0;
+        med0[4 * p + 3] = (unsigned long long)(nc / 2);
+    }
+    CUDA_TRY(cudaMemcpyAsync(d_x, X, nx * 8, cudaMemcpyHostToDevice, st), "copy X");
+    CUDA_TRY(cudaMemcpyAsync(d_w, W, nw * 8, cudaMemcpyHostToDevice, st), "copy W");
+    CUDA_TRY(cudaMemsetAsync(d_sums, 0, (size_t)P * 4 * 8, st), "clear sums");
+    CUDA_TRY(cudaMemcpyAsync(d_med, med0.data(), med0.size() * 8, cudaMemcpyHostToDevice, st),
+             "radix states");
+    drift_policy exact{};
+    exact.input_format = exact.grad_format = DRIFT_FMT_NONE;
+    exact.grad_rounding = DRIFT_ROUND_INHERIT;
+    exact.scale_block = exact.acc_block = 32;
+    exact.acc = DRIFT_ACC_FP64;
+    exact.order = DRIFT_SEQUENTIAL;
+    rc = launch_gemm(ctx->ws, ctx->sched, &exact, M, N, K, d_x, K, 1, d_w, K, 1, nullptr, d_exact,
+                     N, ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st);
+    if (rc) return fail(rc, "exact contraction");
+    for (int64_t k = 0; k < P; k++) {
+        const drift_policy *p = &policies[k];
+        CUDA_TRY(cudaMemcpyAsync(d_state, &rng_seed, 8, cudaMemcpyHostToDevice, st), "rng in");
+        const double *a = d_x, *b = d_w;
+        if (p->input_format != DRIFT_FMT_NONE) {
+            const double *src[2] = {d_x, d_w};
+            double *dst[2] = {d_qx, d_qw};
+            const int64_t n[2] = {nx, nw};
+            // Quant.quantize reads the per-tensor factor only under PER_TENSOR
+            // scaling (Quant.java:63-80), so the amax pass runs only there.
+            const bool per_tensor = p->scaling == DRIFT_PER_TENSOR;
+            for (int t = 0; t < 2; t++) {
+                rc = DRIFT_OK;
+                if (per_tensor) {
+                    rc = launch_amax(src[t], n[t], d_scal, st);
+                    if (!rc) rc = launch_per_tensor_scale(p->input_format, d_scal, d_scal + 1, st);
+                }
+                if (!rc)
+                    rc = launch_quantize(ctx->ws, p, p->input_format, p->input_rounding, src[t],
+                                         dst[t], n[t], per_tensor ? d_scal + 1 : nullptr, 1.0,
+                                         d_state, d_cl + 2 * k + t, ctx->d_err(), st);
+                if (rc) return fail(rc, "cast");
+            }
+            a = d_qx;
+            b = d_qw;
+        }
+        if (stochastic_acc(p))
+            rc = launch_contract(ctx->ws, ctx->sched, p,
+                                 gemm_as_contraction(M, N, K, a, K, 1, b, K, 1, nullptr, d_c, N),
+                                 d_state, ctx->d_err(), st);
+        else
+            rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, a, K, 1, b, K, 1, nullptr, d_c, N,
+                             ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st);
+        if (rc) return fail(rc, "contraction");
+        rc = launch_error_sums(d_c, d_exact, nc, d_sums + 2 * k, st);
+        for (int m = 0; m < 2 && !rc; m++)
+            for (int pass = 0; pass < DRIFT_RADIX_PASSES && !rc; pass++) {
+                rc = launch_radix_pass(d_c, d_exact, nc, pass, d_med + 4 * k + 2 * m, d_hist, st);
+                if (!rc) rc = launch_radix_select(pass, d_hist, d_med + 4 * k + 2 * m, st);
+            }
+        if (rc) return fail(rc, "statistics");
+    }
+    std::vector<double> sums((size_t)P * 2);
+    std::vector<unsigned long long> cl((size_t)P * 2), med((size_t)P * 4);
+    CUDA_TRY(cudaMemcpyAsync(sums.data(), d_sums, sums.size() * 8, cudaMemcpyDeviceToHost, st),
+             "read sums");
+    CUDA_TRY(cudaMemcpyAsync(cl.data(), d_cl, cl.size() * 8, cudaMemcpyDeviceToHost, st),
+             "read clamps");
+    CUDA_TRY(cudaMemcpyAsync(med.data(), d_med, med.size() * 8, cudaMemcpyDeviceToHost, st),
+             "read medians");
+    rc = take_device_error(ctx, st);
+    if (rc) return rc;
+    for (int64_t k = 0; k < P; k++) {
+        const double lo = bitsd(med[4 * k]), hi = bitsd(med[4 * k + 2]);
+        stats_out[4 * k + 0] = 0.5 * (lo + hi);
+        stats_out[4 * k + 1] = std::sqrt(sums[2 * k] / sums[2 * k + 1]);
+        stats_out[4 * k + 2] = (double)cl[2 * k];
+        stats_out[4 * k + 3] = (double)cl[2 * k + 1];
+    }
+    return DRIFT_OK;
+}
+
 // ------------------------------------------------------------------ device-resident calls
 
 int drift_amax_dev(drift_ctx *ctx, const double *d_x, int64_t n, double *d_amax, void *stream) {

@@ -1,7 +1,7 @@
 // stats.cu — error statistics of an emulated GEMM against its exact twin.
 //
 // RealDotSweep reports, per policy, the RMS of (got - exact) over the RMS of
-// exact (java/src/main/java/io/drift/tools/RealDotSweep.java:245-257, :264-270).
+// exact (java/src/main/java/io/drift/tools/RealDotSweep.java:130-142, :149-155).
 // One pass reads both outputs once (16 bytes per output element) and adds
 // sum((got-exact)^2) and sum(exact^2) into two device doubles. The sums are
 // reductions of squares, reported with a relative tolerance; the emulated
@@ -56,7 +56,7 @@ int launch_error_sums(const double *got, const double *exact, int64_t n, double 
 // ------------------------------------------------------------------ exact order statistics
 //
 // The k-th smallest relative error |got - exact| / |exact| (the median of
-// DotSweep.java:152-153 and RealDotSweep.java:255-256) over all outputs, found
+// DotSweep.java:152-153 and RealDotSweep.java:140-141) over all outputs, found
 // by radix selection on the double's bit pattern: for non-negative doubles
 // the bits order like the values, and NaN (0/0) is mapped above +Inf, where
 // Java's sort puts it. Six passes of 11, 11, 11, 11, 11 and 9 bits each read

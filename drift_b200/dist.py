@@ -84,7 +84,7 @@ def finish(dist) -> None:
 
 
 def rms_ratio(err_sq: float, exact_sq: float) -> Optional[float]:
-    """RealDotSweep's RMS ratio (RealDotSweep.java:257, :264-270) from sums."""
+    """RealDotSweep's RMS ratio (RealDotSweep.java:142, :149-155) from sums."""
     import math
 
     if exact_sq <= 0.0:

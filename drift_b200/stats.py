@@ -1,8 +1,8 @@
 """Statistics of an emulated GEMM against its exact twin, on the device.
 
-RMS ratio (RealDotSweep.java:257, :264-270) from two sums, and exact order
+RMS ratio (RealDotSweep.java:142, :149-155) from two sums, and exact order
 statistics of the relative error (the medians of DotSweep.java:152-153 and
-RealDotSweep.java:255-256) by radix selection. With a process group, every
+RealDotSweep.java:140-141) by radix selection. With a process group, every
 rank's outputs take part: the per-pass histograms and the sums are
 all-reduced, so all ranks select the same element.
 """

@@ -219,7 +219,7 @@ def dot_sweep_dev(lengths: Sequence[int] = tuple(2 ** k for k in range(4, 13)),
 def real_dot_policies() -> List[NumericPolicy]:
     """The real-shape batch's 7 policies: FP32/FP16/BF16 sequential, FP16/BF16
     pairwise, the e4m3 per-tensor cast and the bf16 cast (from
-    RealDotSweep.java:212-223)."""
+    RealDotSweep.java:97-108)."""
     b = NumericPolicy.builder
     return [b("fp32 sequential").build(),
             b("fp16 sequential").acc(Acc.FP16).build(),
@@ -232,7 +232,7 @@ def real_dot_policies() -> List[NumericPolicy]:
 
 def real_dot_inputs(seed: int = 424242, windows: int = 4096, units: int = 64, ctx: int = 32,
                     emb: int = 64, vocab: int = 96):
-    """Synthetic stand-ins for RealDotSweep's tensors (RealDotSweep.java:191-201):
+    """Synthetic stand-ins for RealDotSweep's tensors (RealDotSweep.java:78-86):
     X = windows of an N(0,1) embedding table picked by uniform tokens (64 groups
     of 64 windows); W = Kaiming-normal rows, std sqrt(2 / fan_in)."""
     rs = np.random.default_rng(seed)
@@ -279,7 +279,7 @@ def policy_outputs(p: NumericPolicy, X: np.ndarray, W: np.ndarray, rng_seed: int
 
 def real_dot_batch(X=None, W=None, policies=None) -> Dict[str, Dict[str, float]]:
     """The real-shape batch: per policy, the true median relative error and the
-    RMS ratio over all windows x units (RealDotSweep.java:245-257)."""
+    RMS ratio over all windows x units (RealDotSweep.java:130-142)."""
     if X is None:
         X, W = real_dot_inputs()
     policies = policies or real_dot_policies()
@@ -299,7 +299,7 @@ def real_dot_batch(X=None, W=None, policies=None) -> Dict[str, Dict[str, float]]
 def real_dot_batch_dev(X=None, W=None, policies=None, device: int = 0) -> Dict:
     """real_dot_batch on the device: X and W cross to the GPU once; per policy
     the whole-tensor per-tensor scales, the casts of X then W on the policy's
-    Rng(7) (RealDotSweep.java:235-254), the contraction, the true median of
+    Rng(7) (RealDotSweep.java:119-128), the contraction, the true median of
     the relative errors (two radix selections) and the RMS sums, all on the
     device; one read-back at the end. The medians are exact order statistics
     of bit-exact outputs; the RMS ratio comes from a parallel sum, so it
@@ -350,6 +350,37 @@ def real_dot_batch_dev(X=None, W=None, policies=None, device: int = 0) -> Dict:
         out[p.name] = {"median_rel_error": 0.5 * (lo + hi),
                        "rms_error_ratio": float(np.sqrt(s[k, 0] / s[k, 1]))}
     return out
+
+
+def real_dot_sweep(X=None, W=None, policies=None, rng_seed: int = 7) -> Dict:
+    """RealDotSweep's whole policy loop (:235-257) in one host-buffer C-ABI
+    call: X and W cross to the device once, every policy's casts, contraction,
+    median and RMS sums run there, and only four numbers per policy come back:
+    the true median relative error, the RMS ratio and the clamp counts of the
+    casts of X and of W."""
+    import ctypes
+
+    from . import _lib
+
+    if X is None:
+        X, W = real_dot_inputs()
+    policies = policies or real_dot_policies()
+    X = np.ascontiguousarray(X, dtype=np.float64)
+    W = np.ascontiguousarray(W, dtype=np.float64)
+    M, K = X.shape
+    N, K2 = W.shape
+    if K2 != K:
+        raise ValueError(f"X is {M}x{K} but W is {N}x{K2}")
+    P = len(policies)
+    pols = (_lib.DriftPolicy * max(P, 1))(*[p.to_c() for p in policies])
+    stats = np.zeros((max(P, 1), 4), dtype=np.float64)
+    _lib.check(_lib.load().drift_real_dot_sweep(
+        _lib.Context.current().handle, ctypes.cast(pols, ctypes.c_void_p), P, M, N, K,
+        X.ctypes.data, W.ctypes.data, ctypes.c_uint64(rng_seed), stats.ctypes.data))
+    return {p.name: {"median_rel_error": float(stats[k, 0]),
+                     "rms_error_ratio": float(stats[k, 1]),
+                     "clamped_x": int(stats[k, 2]), "clamped_w": int(stats[k, 3])}
+            for k, p in enumerate(policies)}
 
 
 def mx_policies() -> List[NumericPolicy]:
@@ -447,7 +478,7 @@ def mx_gemm(size: int = 4096, seed: int = 0, policies=None, device: int = 0, dis
 # ------------------------------------------------------------------ policy sweep
 
 def policy_sweep_policies() -> List[NumericPolicy]:
-    """RealDotSweep's policy list (RealDotSweep.java:212-223): the 9
+    """RealDotSweep's policy list (RealDotSweep.java:97-108): the 9
     accumulator x order policies (blocked in chunks of 32), the bf16 cast,
     e4m3 per-tensor and e4m3 MX32, each with its cast of both operands."""
     b = NumericPolicy.builder

@@ -200,7 +200,7 @@ DRIFT_API int drift_quantize(drift_ctx *ctx, const drift_policy *p, int fmt,
  * for i in [0,M), o in [0,N): the double loops of
  * java/.../train/Pass.java:200-204 (forward), :222-226 (dgrad, B strided),
  * :228-232 (wgrad, both strided), java/.../tools/DotSweep.java:121 (M=N=1)
- * and java/.../tools/RealDotSweep.java:247-254. Dot.dot itself is
+ * and java/.../tools/RealDotSweep.java:132-139. Dot.dot itself is
  * java/.../kernel/Dot.java:26-121. Strides may be any non-negative values.
  * With a STOCHASTIC accumulator the dots draw from *rng_state in (i, o) order
  * and in each dot's evaluation order, only for inexact sums, exactly as the
@@ -351,7 +351,7 @@ DRIFT_API int drift_gemm_route(drift_ctx *ctx, int *route, void *stream);
 DRIFT_API int drift_set_thin_tiles(drift_ctx *ctx, int64_t tiles);
 
 /* Error sums of RealDotSweep's RMS ratio
- * (java/.../tools/RealDotSweep.java:245-257): ADDS sum((got-exact)^2) to
+ * (java/.../tools/RealDotSweep.java:130-142): ADDS sum((got-exact)^2) to
  * d_sums[0] and sum(exact^2) to d_sums[1]. */
 DRIFT_API int drift_error_sums_dev(drift_ctx *ctx, const double *d_got,
                                    const double *d_exact, int64_t n,
@@ -360,7 +360,7 @@ DRIFT_API int drift_error_sums_dev(drift_ctx *ctx, const double *d_got,
 /*
  * Exact order statistics of the relative error |got - exact| / |exact| over
  * all n outputs (the medians of java/.../tools/DotSweep.java:152-153 and
- * RealDotSweep.java:255-256), by radix selection on the double's bits in
+ * RealDotSweep.java:140-141), by radix selection on the double's bits in
  * DRIFT_RADIX_PASSES passes. d_state holds two uint64: the digits chosen so
  * far (start at 0) and the 0-based rank sought (start at k). Each pass:
  * drift_radix_hist_dev clears d_hist (DRIFT_RADIX_BINS uint64) and counts the
@@ -393,6 +393,28 @@ DRIFT_API int drift_group_kth_rel_error_dev(drift_ctx *ctx, const double *d_got,
                                             const double *d_exact, int64_t groups,
                                             int64_t n, int64_t k, double *d_out,
                                             void *stream);
+
+/*
+ * RealDotSweep's per-policy loop (java/.../tools/RealDotSweep.java:119-142) in
+ * one call on host tensors: X (M x K) and W (N x K), row-major, cross to the
+ * device once; the exact FP64 contraction (:88-95); then for each of
+ * n_policies policies, in order: an Rng seeded rng_seed (:122), the
+ * whole-tensor per-tensor scales (Quant.perTensorScale of Quant.amax, :125-126;
+ * computed only under PER_TENSOR scaling, the one that reads them), the casts
+ * of X then W (Quant.quantize with the policy's input format, rounding and
+ * scaling, :127-128), the contraction (Dot.dot over every (row of X, row of W)
+ * pair, :132-139), and its statistics against the exact outputs.
+ * stats_out[4p .. 4p+3] receives, for policy p: the true median of
+ * |got - exact| / |exact| (the mean of the two middle values, :140-141), the
+ * RMS ratio sqrt(sum (got-exact)^2 / sum exact^2) (:142, :149-155; a parallel
+ * sum, so equal to the sequential one to rounding), the clamp count of X's
+ * cast and of W's. Only the statistics come back. Returns when they are in
+ * stats_out.
+ */
+DRIFT_API int drift_real_dot_sweep(drift_ctx *ctx, const drift_policy *policies,
+                                   int n_policies, int64_t M, int64_t N, int64_t K,
+                                   const double *X, const double *W, uint64_t rng_seed,
+                                   double *stats_out);
 
 /* ----------------------------------------------------------- diagnostics */
 /*

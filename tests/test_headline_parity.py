@@ -3,7 +3,7 @@
 The sweep's GEMM is M = N = K = 8192 on N(0,1) x lognormal(0,1) doubles with
 full 53-bit significands (generated on the device by the same seeded generator
 the bench uses), under RealDotSweep's 12 policies
-(java/src/main/java/io/drift/tools/RealDotSweep.java:212-223) plus the FP64
+(java/src/main/java/io/drift/tools/RealDotSweep.java:97-108) plus the FP64
 exact GEMM. Every contraction runs on the device at full size, on the route
 it takes in the sweep (the double-precision tiled kernel, or the FP32 pipe for
 the bf16 and MX-e4m3 casts); then a sample of 16 rows x 128 columns of each

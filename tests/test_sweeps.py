@@ -51,20 +51,21 @@ def test_real_shape_batch_every_output():
     X, W = sweeps.real_dot_inputs()
     M, K = X.shape
     N = W.shape[0]
+    clamps = {}
     for p in sweeps.real_dot_policies():
         got, clamped = sweeps.policy_outputs(p, X, W)
         f = p.input_format
         fid = f.id if f is not None else -1
-        qx, qw, cl = X, W, 0
+        qx, qw, c1, c2 = X, W, 0, 0
         rng = 7
         if f is not None:
             op = _op(p)
             qx, c1, rng = O.quantize(op, fid, 0, X.reshape(-1), O.per_tensor_scale(fid, O.amax(X)), rng)
             qw, c2, rng = O.quantize(op, fid, 0, W.reshape(-1), O.per_tensor_scale(fid, O.amax(W)), rng)
-            cl = c1 + c2
         want, _ = O.gemm(_op(p), M, N, K, qx, 0, K, 1, qw, 0, K, 1, threads=16)
         assert (got.view(np.int64) == want.view(np.int64)).all(), p.name
-        assert clamped == cl
+        assert clamped == c1 + c2
+        clamps[p.name] = (c1, c2)
     stats = sweeps.real_dot_batch(X, W)
     assert stats["fp32 sequential"]["median_rel_error"] < stats["bf16 sequential"]["median_rel_error"]
     # The device-resident driver: the same true medians bit for bit (order
@@ -75,6 +76,67 @@ def test_real_shape_batch_every_output():
         assert dev[name]["median_rel_error"] == stats[name]["median_rel_error"], name
         assert dev[name]["rms_error_ratio"] == pytest.approx(stats[name]["rms_error_ratio"],
                                                              rel=1e-12), name
+    # The whole loop in one host-buffer call: the same statistics, and the
+    # clamp counts of each operand's cast.
+    one = sweeps.real_dot_sweep(X, W)
+    assert one.keys() == stats.keys()
+    for name in stats:
+        assert one[name]["median_rel_error"] == stats[name]["median_rel_error"], name
+        assert one[name]["rms_error_ratio"] == pytest.approx(stats[name]["rms_error_ratio"],
+                                                             rel=1e-12), name
+        assert (one[name]["clamped_x"], one[name]["clamped_w"]) == clamps[name], name
+
+
+def _oracle_real_dot_stats(p, X, W, seed):
+    """RealDotSweep's per-policy flow (:235-257) on the oracle: Rng(seed), the
+    per-tensor casts of X then W, the contraction on the same Rng, the true
+    median and the RMS ratio against the FP64 outputs."""
+    from drift_b200.kernel import NumericPolicy
+
+    M, K = X.shape
+    N = W.shape[0]
+    op = _op(p)
+    f = p.input_format
+    rng, qx, qw, c1, c2 = seed, X.reshape(-1), W.reshape(-1), 0, 0
+    if f is not None:
+        rm = int(p.input_rounding)
+        qx, c1, rng = O.quantize(op, f.id, rm, qx, O.per_tensor_scale(f.id, O.amax(X)), rng)
+        qw, c2, rng = O.quantize(op, f.id, rm, qw, O.per_tensor_scale(f.id, O.amax(W)), rng)
+    got, _ = O.gemm(op, M, N, K, qx, 0, K, 1, qw, 0, K, 1, rng_state=rng, threads=8)
+    ex, _ = O.gemm(_op(NumericPolicy.exact()), M, N, K, X, 0, K, 1, W, 0, K, 1, threads=8)
+    err = (got - ex).reshape(-1)
+    rel = np.sort(np.abs(err) / np.abs(ex.reshape(-1)))
+    n = rel.size
+    return (0.5 * (rel[n // 2 - 1] + rel[n // 2]),
+            np.sqrt(np.sum(err * err) / np.sum(ex * ex)), c1, c2)
+
+
+def test_real_dot_sweep_stochastic_policies_against_oracle():
+    """The one-call loop on policies the real-shape batch does not hold:
+    stochastic casts, stochastic accumulation (the contraction kernels'
+    Rng path), blocked order, a format that clamps, a seed other than 7."""
+    from drift_b200 import sweeps
+    from drift_b200.fmt import Formats, Rounding
+    from drift_b200.kernel import Acc, NumericPolicy, Order, Scaling
+
+    b = NumericPolicy.builder
+    pols = [b("e4m3 sr cast").input(Formats.E4M3).input_rounding(Rounding.STOCHASTIC)
+            .scaling(Scaling.PER_TENSOR).build(),
+            b("bf16 sr acc").acc(Acc.BF16).acc_rounding(Rounding.STOCHASTIC).build(),
+            b("fp16 sr acc blocked").acc(Acc.FP16).order(Order.BLOCKED)
+            .acc_rounding(Rounding.STOCHASTIC).build(),
+            b("e2m1 truncated").input(Formats.E2M1).input_rounding(Rounding.TRUNCATE).build(),
+            b("fp32 reversed").order(Order.REVERSED).build()]
+    rs = np.random.default_rng(5)
+    X = rs.standard_normal((96, 320)) * np.exp(rs.standard_normal((96, 320)))
+    W = rs.standard_normal((40, 320))
+    one = sweeps.real_dot_sweep(X, W, pols, rng_seed=1234)
+    for p in pols:
+        med, rms, c1, c2 = _oracle_real_dot_stats(p, X, W, 1234)
+        got = one[p.name]
+        assert got["median_rel_error"] == med, p.name
+        assert got["rms_error_ratio"] == pytest.approx(rms, rel=1e-12), p.name
+        assert (got["clamped_x"], got["clamped_w"]) == (c1, c2), p.name
 
 
 def test_mx_gemm_sampled_outputs():
