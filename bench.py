@@ -238,14 +238,13 @@ def run_engine(args):
     gemm_ms = [0.0] * (n_pol + 1)
     launches = [0]
     # Each contraction's route (drift_gemm_route), read in the first warm-up
-    # step: routes 0 (tiled) and 3 (one output per thread) are one launch;
-    # routes 1 (FP32 pipe) and 2 (scanned, stayed on the double-precision
-    # kernels) are five (two operand scans, the decision, and both
-    # contractions, one of which stands down at once).
+    # step. The kernels each GEMM call queued (operand scans, decisions and
+    # both builds of a scanned route, one of which stands down at once) come
+    # from drift_gemm_launches, a host-side count read after every call.
     routes = [None] * (n_pol + 1)
 
-    def gemm_launches(k):
-        return 5 if routes[k] in (d.ROUTE_FP32, d.ROUTE_SCANNED) else 1
+    def gemm_launches():
+        return d.gemm_launches(ctx=ctx)
 
     # The cast pass's own device time (the quantize launch of each cast policy's
     # A operand, last step), for its HBM roofline.
@@ -280,7 +279,7 @@ def run_engine(args):
         ev[0][1].record(stream)
         if read_routes:
             routes[0] = d.gemm_route(ctx=ctx)
-        launches[0] += gemm_launches(0)
+        launches[0] += gemm_launches()
         for k, p in enumerate(pols):
             a = cast(p, A, qA, 0, clamps[k, 0:1], k)
             b = cast(p, B, qB, 1, clamps[k, 1:2])
@@ -289,7 +288,7 @@ def run_engine(args):
             ev[k + 1][1].record(stream)
             if read_routes:
                 routes[k + 1] = d.gemm_route(ctx=ctx)
-            launches[0] += gemm_launches(k + 1) - 1
+            launches[0] += gemm_launches() - 1
             d.error_sums_dev(C, Cx, sums[k], ctx=ctx)
             # DotSweep's summary statistic over every rank's outputs: the upper
             # median of the relative errors (DotSweep.java:152-153).

@@ -11,15 +11,15 @@ from ._lib import Context, DriftError
 from .fmt import Formats, MiniFloat, Rng, Rounding, Specials
 from .kernel import (Acc, Dot, NumericPolicy, Order, Quant, Scaling, Window, amax_dev,
                      check_dev, contract, contract_dev, contraction, error_sums_dev, gemm,
-                     per_tensor_scale_dev, probe_fp32, probe_fp64, gemm_dev, gemm_route,
-                     quantize_dev, set_thin_tiles, ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED,
-                     ROUTE_STAGED)
+                     per_tensor_scale_dev, probe_fp32, probe_fp64, gemm_dev, gemm_launches,
+                     gemm_route, quantize_dev, set_thin_tiles, ROUTE_DOUBLE, ROUTE_FP32,
+                     ROUTE_SCANNED, ROUTE_STAGED, ROUTE_PROVEN)
 from . import policies
 
 _lib.load()
 
 __all__ = ["Context", "DriftError", "Formats", "MiniFloat", "Rng", "Rounding", "Specials", "Acc",
            "Dot", "NumericPolicy", "Order", "Quant", "Scaling", "Window", "contraction", "contract",
-           "contract_dev", "gemm", "gemm_dev", "gemm_route", "quantize_dev", "ROUTE_DOUBLE",
-           "ROUTE_FP32", "ROUTE_SCANNED", "ROUTE_STAGED", "set_thin_tiles",
+           "contract_dev", "gemm", "gemm_dev", "gemm_launches", "gemm_route", "quantize_dev",
+           "ROUTE_DOUBLE", "ROUTE_FP32", "ROUTE_SCANNED", "ROUTE_STAGED", "ROUTE_PROVEN", "set_thin_tiles",
            "amax_dev", "check_dev", "policies"]

@@ -92,6 +92,7 @@ SIGNATURES = {
     "drift_gemm_dev": (_int, [_vp, _P(DriftPolicy), _i64, _i64, _i64, _vp, _i64, _i64, _vp,
                               _i64, _i64, _vp, _vp, _i64, _vp, _vp]),
     "drift_gemm_route": (_int, [_vp, _P(_int), _vp]),
+    "drift_gemm_launches": (_int, [_vp, _P(_int)]),
     "drift_set_thin_tiles": (_int, [_vp, _i64]),
     "drift_error_sums_dev": (_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "drift_radix_hist_dev": (_int, [_vp, _vp, _vp, _i64, _int, _vp, _vp, _vp]),

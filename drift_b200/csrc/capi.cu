@@ -147,13 +147,16 @@ struct drift_ctx {
     Workspace io;       // staging for host-buffer calls
     ScheduleCache sched;
     // Small device words: [0] error flags (int), [8] rng state, [16] clamp
-    // counter, [24] scalar result, [32] the last GEMM's route (int).
+    // counter, [24] scalar result, [32] the last GEMM's route (int), [64] the
+    // range proof's eight operand-scan words.
     char *d_small = nullptr;
     int *d_err() { return (int *)d_small; }
     uint64_t *d_state() { return (uint64_t *)(d_small + 8); }
     unsigned long long *d_clamped() { return (unsigned long long *)(d_small + 16); }
     double *d_scalar() { return (double *)(d_small + 24); }
     int *d_route() { return (int *)(d_small + 32); }
+    unsigned *d_scan() { return (unsigned *)(d_small + 64); }
+    int last_launches = 0;  // kernels the last GEMM queued (drift_gemm_launches)
     int64_t thin_tiles = -1;  // drift_set_thin_tiles; negative: two per SM
 };
 
@@ -245,8 +248,8 @@ int drift_open(int device, drift_ctx **out) {
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_b[c], cudaEventDisableTiming);
     }
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_start, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_small, 64);
-    if (e == cudaSuccess) e = cudaMemset(ctx->d_small, 0, 64);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_small, 128);
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_small, 0, 128);
     if (e != cudaSuccess) {
         for (int c = 0; c < kPipeChunks; c++) {
             if (ctx->ev_in[c]) cudaEventDestroy(ctx->ev_in[c]);
@@ -640,14 +643,16 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
                     rc = launch_gemm(ctx->ws, ctx->sched, p, rows, cols, K, d_a + off, a_row_stride,
                                      1, d_b + j0 * b_row_stride, b_row_stride, 1,
                                      d_bias ? d_bias + j0 : nullptr, d_c + r0 * N + j0, N,
-                                     ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st);
+                                     ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st,
+                                     ctx->d_scan(), &ctx->last_launches);
                     if (rc) rc = fail(rc, "gemm launch");
                 }
                 if (rc) break;
             } else {
                 rc = launch_gemm(ctx->ws, ctx->sched, p, rows, N, K, d_a + off, a_row_stride, 1,
                                  d_b, b_row_stride, b_k_stride, d_bias, d_c + r0 * N, N,
-                                 ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st);
+                                 ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st,
+                                 ctx->d_scan(), &ctx->last_launches);
                 if (rc) {
                     rc = fail(rc, "gemm launch");
                     break;
@@ -676,7 +681,7 @@ int drift_gemm(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, int6
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_a, a_row_stride, a_k_stride, d_b,
                          b_row_stride, b_k_stride, d_bias, d_c, N, ctx->thin_tiles, ctx->d_err(),
-                         ctx->d_route(), st);
+                         ctx->d_route(), st, ctx->d_scan(), &ctx->last_launches);
     }
     if (rc) return fail(rc, "gemm launch");
     CUDA_TRY(cudaMemcpy2DAsync(C, c_row_stride * 8, d_c, N * 8, N * 8, M, cudaMemcpyDeviceToHost, st),
@@ -744,7 +749,8 @@ int drift_real_dot_sweep(drift_ctx *ctx, const drift_policy *policies, int n_pol
     exact.acc = DRIFT_ACC_FP64;
     exact.order = DRIFT_SEQUENTIAL;
     rc = launch_gemm(ctx->ws, ctx->sched, &exact, M, N, K, d_x, K, 1, d_w, K, 1, nullptr, d_exact,
-                     N, ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st);
+                     N, ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st,
+                     ctx->d_scan(), &ctx->last_launches);
     if (rc) return fail(rc, "exact contraction");
     for (int64_t k = 0; k < P; k++) {
         const drift_policy *p = &policies[k];
@@ -778,7 +784,8 @@ int drift_real_dot_sweep(drift_ctx *ctx, const drift_policy *policies, int n_pol
                                  d_state, ctx->d_err(), st);
         else
             rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, a, K, 1, b, K, 1, nullptr, d_c, N,
-                             ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st);
+                             ctx->thin_tiles, ctx->d_err(), ctx->d_route(), st,
+                             ctx->d_scan(), &ctx->last_launches);
         if (rc) return fail(rc, "contraction");
         rc = launch_error_sums(d_c, d_exact, nc, d_sums + 2 * k, st);
         for (int m = 0; m < 2 && !rc; m++)
@@ -889,7 +896,8 @@ int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M, int64_t N, 
     } else {
         rc = launch_gemm(ctx->ws, ctx->sched, p, M, N, K, d_A, a_row_stride, a_k_stride, d_B,
                          b_row_stride, b_k_stride, d_bias, d_C, c_row_stride, ctx->thin_tiles,
-                         ctx->d_err(), ctx->d_route(), pick(ctx, stream));
+                         ctx->d_err(), ctx->d_route(), pick(ctx, stream), ctx->d_scan(),
+                         &ctx->last_launches);
     }
     return rc ? fail(rc, "gemm launch") : DRIFT_OK;
 }
@@ -898,6 +906,14 @@ int drift_set_thin_tiles(drift_ctx *ctx, int64_t tiles) {
     int rc = enter(ctx);
     if (rc) return rc;
     ctx->thin_tiles = tiles < 0 ? -1 : tiles;
+    return DRIFT_OK;
+}
+
+int drift_gemm_launches(drift_ctx *ctx, int *launches) {
+    int rc = enter(ctx);
+    if (rc) return rc;
+    if (!launches) return fail(DRIFT_EINVAL, "null launches");
+    *launches = ctx->last_launches;
     return DRIFT_OK;
 }
 

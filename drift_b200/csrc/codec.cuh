@@ -292,11 +292,14 @@ struct FastForm {
         const double d = __hiloint2double((int)dh, prev_lo);
         return __fma_rn(d, -kScale, __fma_rn(d, kScale, t));
     }
-    // Round toward zero (SHIFT >= 32: only the high word holds dropped bits;
-    // prev_lo is zero for the narrow accumulators that use this).
-    __device__ static __forceinline__ double trunc(double t, int prev_lo, unsigned &range) {
+    // Round toward zero (SHIFT >= 32: only the high word holds kept bits, and
+    // the low word of the result is zero). The low word is written as a
+    // constant rather than carried over from the accumulator register: with
+    // the carried form, a blocked contraction on the schedule-driven path
+    // returned sums that differ from Dot.round's on B200.
+    __device__ static __forceinline__ double trunc(double t, int, unsigned &range) {
         range = exp_word(t) - kBase;
-        return __hiloint2double(__double2hiint(t) & ~((1 << (SHIFT - 32)) - 1), prev_lo);
+        return __hiloint2double(__double2hiint(t) & ~((1 << (SHIFT - 32)) - 1), 0);
     }
     // Folds two range words into a group's running max.
     __device__ static __forceinline__ unsigned fold2(unsigned run, unsigned r0, unsigned r1) {

@@ -47,6 +47,7 @@
 // checked once per k. Either way the schedule is the same for every output,
 // so control flow is uniform across the CTA.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <type_traits>
 #include <vector>
@@ -93,6 +94,14 @@ constexpr int kp_unroll() {
 
 enum SegMode { SEG_NONE = 0, SEG_TILE = 1, SEG_SCHED = 2 };
 
+// The accumulator rounding of a contraction. PROVEN: an operand scan showed
+// that every sum of this call stays inside the fast form's exact range (see
+// range_proven below), so no sum is checked and no group is ever redone.
+template <int ACC, int RM, bool PROVEN>
+struct GemmRound : AccRound<ACC, RM> {
+    __device__ static bool valid(unsigned run) { return PROVEN || AccRound<ACC, RM>::valid(run); }
+};
+
 struct GemmArgs {
     int64_t M, N, K;
     const double *A;
@@ -114,6 +123,13 @@ struct GemmArgs {
     // When set, the kernel leaves at once if the word reads nonzero: the FP32
     // path (gemm32.cu) took the call.
     const int *skip;
+    // When set, the operand scan's words (range_scan_kernel): the PROVEN
+    // build runs if they prove the call's range, the checked build otherwise,
+    // and the other leaves at once. range_limit bounds the sum of the two
+    // operands' top exponents (range_limit_for).
+    const unsigned *range;
+    int range_limit;
+    int *route;  // receives DRIFT_ROUTE_PROVEN from the PROVEN build when it runs
 };
 
 // Offset, in doubles, of element (row, k) of a staged operand tile.
@@ -139,10 +155,10 @@ constexpr int mac_group() {
 // group's sums exactly from the kept sums.
 // FIRST starts a fresh sum: acc = round(0.0 + a_i * b_j), whatever acc held
 // (0.0 + p is not p when p is -0.0, so the add stays).
-template <int ACC, int RM, int G = GROUP_ROWS, bool FIRST = false>
+template <int ACC, int RM, int G = GROUP_ROWS, bool FIRST = false, bool PV = false>
 __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[TM],
                                       const double (&b)[TN]) {
-    using R = AccRound<ACC, RM>;
+    using R = GemmRound<ACC, RM, PV>;
     if constexpr (ACC == DRIFT_ACC_FP64) {
 #pragma unroll
         for (int i = 0; i < TM; i++)
@@ -179,10 +195,10 @@ __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[T
 // One k step of a full tile: as mac16, but the sums' range words are folded
 // into `run`, which the caller checks once for the whole tile. No sum is kept
 // for a recompute: a tile that misses is redone from its start (redo_*).
-template <int ACC, int RM, bool FIRST = false>
+template <int ACC, int RM, bool FIRST = false, bool PV = false>
 __device__ __forceinline__ void mac16_run(double (&acc)[TM][TN], const double (&a)[TM],
                                           const double (&b)[TN], unsigned &run) {
-    using R = AccRound<ACC, RM>;
+    using R = GemmRound<ACC, RM, PV>;
 #pragma unroll
     for (int i = 0; i < TM; i++) {
         unsigned u[TN];
@@ -235,9 +251,9 @@ __device__ __forceinline__ void blocked_fold(double (&tot)[TM][TN], double (&acc
 
 // Pairwise combine of the stack top with the current node (Dot.java:97-101):
 // right = round(left + right), validated in groups of GROUP_ROWS rows.
-template <int ACC, int RM>
+template <int ACC, int RM, bool PV = false>
 __device__ __forceinline__ void combine(const double (&left)[TM][TN], double (&right)[TM][TN]) {
-    using R = AccRound<ACC, RM>;
+    using R = GemmRound<ACC, RM, PV>;
 #pragma unroll
     for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
         double t[GROUP_ROWS][TN];
@@ -260,6 +276,119 @@ __device__ __forceinline__ void combine(const double (&left)[TM][TN], double (&r
                 for (int j = 0; j < TN; j++) right[i0 + i][j] = R::exact(t[i][j]);
         }
     }
+}
+
+// ------------------------------------------------------------------ range proof
+//
+// The fast rounding (FastForm) is exact for every sum t with 2^-126 <= |t| <
+// 2^127, the FP32 and BF16 accumulators' normal range below their top binade;
+// the checks exist for the sums outside it. For FP32 and BF16 the operands
+// alone can prove that no sum of a call leaves that range:
+//
+//  - Low side. If every nonzero |a| >= 2^la and |b| >= 2^lb with la + lb >=
+//    -74, every product is zero or at least 2^-74 in magnitude, and its double
+//    is then a multiple of its ulp, at least 2^-126. The sums start at +0, and
+//    a sum or a rounding of multiples of 2^-126 is again one: a double sum
+//    rounds to a coarser grid or is exact, and a value below 2^-103 (FP32) or
+//    2^-119 (BF16) that is a multiple of 2^-126 has at most 24 (8) significant
+//    bits, so the accumulator holds it as is. So a nonzero sum is at least
+//    2^-126. A zero sum is +0: it is x + (-x), or +0 plus a zero, as no
+//    chain value is ever -0 (a nonzero sum never rounds to zero).
+//  - High side. With |a| < 2^(ta+1) and |b| < 2^(tb+1), every product's
+//    double is at most 2^(ta+tb+2), and a sum over k of them, each step rounded
+//    to double and to the accumulator (relative error at most d each), is at
+//    most k * 2^(ta+tb+2) * (1+d)^k. Pairwise nodes and blocked chunks sum
+//    subsets with fewer roundings. range_limit_for bounds ta + tb + 2 so that
+//    this stays at or below 2^126.
+//
+// One scan of each operand gives la, ta and whether it holds Inf, NaN or a
+// subnormal; each contraction build reads the words and either runs or
+// leaves, so the decision never waits on the host.
+
+constexpr int kRangeWords = 4;  // per operand: top exponent field, 2047 - lowest, bad, unused
+// Below this many multiply-accumulates the scan's launch costs more than the
+// checks it removes.
+constexpr double kRangeMinMacs = 134217728.0;  // 2^27
+
+// Folds one element into the scan maxima: [0] largest biased exponent,
+// [1] 2047 - smallest biased exponent of a nonzero element, [2] Inf, NaN or a
+// subnormal seen. Zeros are skipped; an operand of zeros leaves [0] == 0.
+__device__ __forceinline__ void range_fold(double x, unsigned &top, unsigned &low, unsigned &bad) {
+    const unsigned hi = (unsigned)__double2hiint(x) & 0x7FFFFFFFu;
+    const unsigned ef = hi >> 20;
+    if (ef == 0x7FF || (ef == 0 && (hi | (unsigned)__double2loint(x)) != 0)) bad = 1;
+    if (ef != 0 && ef != 0x7FF) {
+        top = max(top, ef);
+        low = max(low, 2047u - ef);
+    }
+}
+
+// Scans operand blockIdx.y (0: A with rows_a rows, 1: B with rows_b) into
+// words[4 * y ..]. Rows are K long, element (r, k) at X[r*rs + k*ks].
+// Contiguous operands are read 16 bytes at a time.
+__global__ void __launch_bounds__(256) range_scan_kernel(const double *A, int64_t rows_a,
+                                                         int64_t a_rs, int64_t a_ks,
+                                                         const double *B, int64_t rows_b,
+                                                         int64_t b_rs, int64_t b_ks, int64_t K,
+                                                         unsigned *words) {
+    const bool second = blockIdx.y == 1;
+    const double *X = second ? B : A;
+    const int64_t rows = second ? rows_b : rows_a, rs = second ? b_rs : a_rs;
+    const int64_t ks = second ? b_ks : a_ks;
+    unsigned top = 0, low = 0, bad = 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const int64_t first = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (ks == 1 && (rs == K || rows == 1)) {  // one contiguous span
+        const int64_t n = rows * K;
+        const bool aligned = ((uintptr_t)X & 15) == 0;
+        const int64_t n2 = aligned ? n / 2 : 0;
+        const double2 *X2 = reinterpret_cast<const double2 *>(X);
+        for (int64_t i = first; i < n2; i += stride) {
+            const double2 v = X2[i];
+            range_fold(v.x, top, low, bad);
+            range_fold(v.y, top, low, bad);
+        }
+        for (int64_t i = 2 * n2 + first; i < n; i += stride) range_fold(X[i], top, low, bad);
+    } else {  // any strides: walk the unit-stride axis innermost
+        const bool kfast = ks == 1 || rs != 1;
+        const int64_t inner = kfast ? K : rows, outer = kfast ? rows : K;
+        const int64_t si = kfast ? ks : rs, so = kfast ? rs : ks;
+        for (int64_t o = blockIdx.x; o < outer; o += gridDim.x)
+            for (int64_t i = threadIdx.x; i < inner; i += blockDim.x)
+                range_fold(X[o * so + i * si], top, low, bad);
+    }
+    top = __reduce_max_sync(0xFFFFFFFFu, top);
+    low = __reduce_max_sync(0xFFFFFFFFu, low);
+    bad = __reduce_max_sync(0xFFFFFFFFu, bad);
+    if ((threadIdx.x & 31) == 0) {
+        unsigned *w = words + (second ? kRangeWords : 0);
+        if (top) atomicMax(&w[0], top);
+        if (low) atomicMax(&w[1], low);
+        if (bad) atomicMax(&w[2], bad);
+    }
+}
+
+// Whether the scan words prove the call's range (see above).
+__device__ __forceinline__ bool range_proven(const unsigned *w, int limit) {
+    const unsigned *a = w, *b = w + kRangeWords;
+    if (a[2] | b[2]) return false;           // Inf, NaN or a subnormal
+    if (a[0] == 0 || b[0] == 0) return true;  // an operand of zeros: every sum is +0
+    const int ta = (int)a[0] - 1023, tb = (int)b[0] - 1023;
+    const int la = 2047 - (int)a[1] - 1023, lb = 2047 - (int)b[1] - 1023;
+    return la + lb >= -74 && ta + tb + 2 <= limit;
+}
+
+// The bound on ta + tb + 2 for K terms: 126 - ceil(log2 K) - ceil(log2 of
+// (1+d)^(K+1)), d the relative error of a double add followed by the
+// accumulator's rounding. Negative when K is too long for any proof.
+static int range_limit_for(int acc, int64_t K) {
+    const double u = acc == DRIFT_ACC_FP32 ? std::ldexp(1.0, -24) : std::ldexp(1.0, -8);
+    const double d = u + std::ldexp(1.0, -53) + u * std::ldexp(1.0, -53);
+    const double growth = (double)(K + 1) * std::log1p(d) / std::log(2.0);
+    if (!(growth < 256.0)) return -1024;
+    int lg = 0;
+    while (lg < 63 && (int64_t(1) << lg) < K) lg++;
+    return 126 - lg - (int)std::ceil(growth + 1e-9);
 }
 
 // One 18 x 64 box of doubles (k0 .. k0+17 of rows r0 .. r0+63) into a tile.
@@ -285,7 +414,7 @@ __device__ __forceinline__ void stage_generic(double *s, const double *X, int64_
 
 // BATCH instantiations read the problem index from blockIdx.z; the others are
 // compiled for one problem, with every batch offset folded away.
-template <int ACC, int ORDER, int RM, int SEG, bool BATCH>
+template <int ACC, int ORDER, int RM, int SEG, bool BATCH, bool PV>
 __global__ void __launch_bounds__(GEMM_THREADS, 2)
     gemm_kernel(const GemmArgs g, const __grid_constant__ CUtensorMap tmA,
                 const __grid_constant__ CUtensorMap tmB) {
@@ -297,6 +426,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
 
     if (g.skip && *g.skip) return;
     const int tid = threadIdx.x;
+    if (g.range) {  // the scan decides which build runs; the other leaves
+        if (range_proven(g.range, g.range_limit) != PV) return;
+        if (PV && g.route && tid == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+            *g.route = DRIFT_ROUTE_PROVEN;
+    }
     const int tx = tid & 15, ty = tid >> 4;
     const int64_t m0 = (int64_t)blockIdx.y * BM;
     const int64_t n0 = (int64_t)blockIdx.x * BN;
@@ -354,7 +488,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
     auto push = [&](int merges, bool fresh = false) {
         for (; merges > 0; merges--) {
             sp--;
-            combine<ACC, RM>(stk[sp], acc);
+            combine<ACC, RM, PV>(stk[sp], acc);
         }
 #pragma unroll
         for (int i = 0; i < TM; i++)
@@ -413,7 +547,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
             // Tile-validated kernels fold the range words of the whole tile
             // into `run` and check it once (a miss redoes the leaves exactly);
             // the others validate each k step's groups (mac16).
-            using R = AccRound<ACC, RM>;
+            using R = GemmRound<ACC, RM, PV>;
             constexpr bool TV = tile_validated<ACC, ORDER>();
             constexpr int G = mac_group<ORDER>();
             unsigned run = 0;
@@ -432,14 +566,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
                 const double by[TN] = {b2[0].y, b2[1].y, b2[2].y, b2[3].y};
                 constexpr bool F = decltype(first)::value;
                 if constexpr (TV) {
-                    mac16_run<ACC, RM, F>(dst, ax, bx, run);
-                    mac16_run<ACC, RM>(dst, ay, by, run);
+                    mac16_run<ACC, RM, F, PV>(dst, ax, bx, run);
+                    mac16_run<ACC, RM, false, PV>(dst, ay, by, run);
                 } else if (REV) {
-                    mac16<ACC, RM, G, F>(dst, ay, by);
-                    mac16<ACC, RM, G>(dst, ax, bx);
+                    mac16<ACC, RM, G, F, PV>(dst, ay, by);
+                    mac16<ACC, RM, G, false, PV>(dst, ax, bx);
                 } else {
-                    mac16<ACC, RM, G, F>(dst, ax, bx);
-                    mac16<ACC, RM, G>(dst, ay, by);
+                    mac16<ACC, RM, G, F, PV>(dst, ax, bx);
+                    mac16<ACC, RM, G, false, PV>(dst, ay, by);
                 }
             };
             // The tile's two pairwise leaves of 8 from zero, exactly.
@@ -469,7 +603,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
 #pragma unroll 1
                 for (int q = BK / 4 + 1; q < BK / 2; q++) kpair(q, acc, Cont{});
                 if (TV && !R::valid(run)) redo_leaves(leaf0, acc);
-                combine<ACC, RM>(leaf0, acc);
+                combine<ACC, RM, PV>(leaf0, acc);
                 push(__ffsll(t + 1) - 1, true);    // ctz(t+1) merges in a perfect tree
             } else {
                 double leaf0[PAIR ? TM : 1][PAIR ? TN : 1];
@@ -493,7 +627,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
                     if (!R::valid(run)) redo_leaves(leaf0, acc);  // rare
                 }
                 if constexpr (PAIR && SEG == SEG_TILE) {
-                    combine<ACC, RM>(leaf0, acc);   // the tile's level-1 node
+                    combine<ACC, RM, PV>(leaf0, acc);   // the tile's level-1 node
                     push(__ffsll(t + 1) - 1);       // ctz(t+1) merges in a perfect tree
                 } else if constexpr (SEG == SEG_TILE && BLOCK) {
                     if (((t + 1) * BK) % g.acc_block == 0) blocked_fold<ACC>(tot, acc);
@@ -509,7 +643,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 2)
                 for (int i = 0; i < TM; i++) a[i] = sA[tile_off(ty + 16 * i, kk)];
 #pragma unroll
                 for (int j = 0; j < TN; j++) b[j] = sB[tile_off(tx + 16 * j, kk)];
-                mac16<ACC, RM, mac_group<ORDER>()>(acc, a, b);
+                mac16<ACC, RM, mac_group<ORDER>(), false, PV>(acc, a, b);
                 after_k();
             }
         }
@@ -574,40 +708,41 @@ int pairwise_schedule(int64_t K, std::vector<uint8_t> &sched, int *depth) {
 
 // ------------------------------------------------------------------ launcher
 
-template <int ACC, int ORDER, int RM, int SEG, bool BATCH>
+template <int ACC, int ORDER, int RM, int SEG, bool BATCH, bool PV>
 static int launch_one(const GemmArgs &g, const CUtensorMap &ma, const CUtensorMap &mb, dim3 grid,
                       cudaStream_t st) {
     // The shared-memory opt-in is per device; setting it is a cheap host call.
-    if (cudaFuncSetAttribute(gemm_kernel<ACC, ORDER, RM, SEG, BATCH>,
+    if (cudaFuncSetAttribute(gemm_kernel<ACC, ORDER, RM, SEG, BATCH, PV>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM) != cudaSuccess)
         return DRIFT_ECUDA;
-    gemm_kernel<ACC, ORDER, RM, SEG, BATCH><<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(g, ma, mb);
+    gemm_kernel<ACC, ORDER, RM, SEG, BATCH, PV><<<grid, GEMM_THREADS, GEMM_SMEM, st>>>(g, ma, mb);
     return DRIFT_OK;
 }
 
-template <int ACC, int RM>
+template <int ACC, int RM, bool PV = false>
 static int launch_order(int order, int seg, const GemmArgs &g, const CUtensorMap &ma,
                         const CUtensorMap &mb, dim3 grid, cudaStream_t st) {
     // Pairwise and blocked run the BATCH build for one problem too: at 8192^3
     // on one B200 it measured 1.1% (fp16) and 1.8% (bf16) faster for pairwise
     // and the same for blocked, while the sequential orders lose about 2% in
     // it and so keep a one-problem build.
-    const bool batch = grid.z > 1;
+    // The PROVEN builds serve one-problem calls only (launch_gemm).
+    const bool batch = grid.z > 1 && !PV;
     switch (order) {
         case DRIFT_SEQUENTIAL:
-            return batch ? launch_one<ACC, DRIFT_SEQUENTIAL, RM, SEG_NONE, true>(g, ma, mb, grid, st)
-                         : launch_one<ACC, DRIFT_SEQUENTIAL, RM, SEG_NONE, false>(g, ma, mb, grid, st);
+            return batch ? launch_one<ACC, DRIFT_SEQUENTIAL, RM, SEG_NONE, !PV, PV>(g, ma, mb, grid, st)
+                         : launch_one<ACC, DRIFT_SEQUENTIAL, RM, SEG_NONE, false, PV>(g, ma, mb, grid, st);
         case DRIFT_REVERSED:
-            return batch ? launch_one<ACC, DRIFT_REVERSED, RM, SEG_NONE, true>(g, ma, mb, grid, st)
-                         : launch_one<ACC, DRIFT_REVERSED, RM, SEG_NONE, false>(g, ma, mb, grid, st);
+            return batch ? launch_one<ACC, DRIFT_REVERSED, RM, SEG_NONE, !PV, PV>(g, ma, mb, grid, st)
+                         : launch_one<ACC, DRIFT_REVERSED, RM, SEG_NONE, false, PV>(g, ma, mb, grid, st);
         case DRIFT_PAIRWISE:
             return seg == SEG_TILE
-                       ? launch_one<ACC, DRIFT_PAIRWISE, RM, SEG_TILE, true>(g, ma, mb, grid, st)
-                       : launch_one<ACC, DRIFT_PAIRWISE, RM, SEG_SCHED, true>(g, ma, mb, grid, st);
+                       ? launch_one<ACC, DRIFT_PAIRWISE, RM, SEG_TILE, true, PV>(g, ma, mb, grid, st)
+                       : launch_one<ACC, DRIFT_PAIRWISE, RM, SEG_SCHED, true, PV>(g, ma, mb, grid, st);
         case DRIFT_BLOCKED:
             return seg == SEG_TILE
-                       ? launch_one<ACC, DRIFT_BLOCKED, RM, SEG_TILE, true>(g, ma, mb, grid, st)
-                       : launch_one<ACC, DRIFT_BLOCKED, RM, SEG_SCHED, true>(g, ma, mb, grid, st);
+                       ? launch_one<ACC, DRIFT_BLOCKED, RM, SEG_TILE, true, PV>(g, ma, mb, grid, st)
+                       : launch_one<ACC, DRIFT_BLOCKED, RM, SEG_SCHED, true, PV>(g, ma, mb, grid, st);
         default: return DRIFT_EINVAL;
     }
 }
@@ -637,12 +772,15 @@ static int gemm_batched(ScheduleCache &cache, const drift_policy *p, int64_t bat
                         int64_t N, int64_t K, const double *A, int64_t a_rs, int64_t a_ks,
                         int64_t a_bs, const double *B, int64_t b_rs, int64_t b_ks, int64_t b_bs,
                         const double *bias, double *C, int64_t c_rs, int64_t c_bs, int *d_err,
-                        const int *skip, cudaStream_t st);
+                        const int *skip, cudaStream_t st, const unsigned *range = nullptr,
+                        int *route = nullptr, int *n_launched = nullptr);
 
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
-                int64_t thin_tiles, int *d_err, int *d_route, cudaStream_t st) {
+                int64_t thin_tiles, int *d_err, int *d_route, cudaStream_t st, unsigned *d_scan,
+                int *n_launched) {
+    if (n_launched) *n_launched = 0;
     if (M < 0 || N < 0 || K < 0 || a_rs < 0 || a_ks < 0 || b_rs < 0 || b_ks < 0 || c_rs < 0 ||
         p->acc < 0 || p->acc > 3 || p->order < 0 || p->order > 3)
         return DRIFT_EINVAL;
@@ -653,6 +791,7 @@ int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int6
     int rc = launch_gemm_f32(ws, p, M, N, K, A, a_rs, a_ks, B, b_rs, b_ks, bias, C, c_rs, d_err,
                              d_route, st, &skip);
     if (rc) return rc;
+    if (skip && n_launched) *n_launched += 4;  // two scans, the decision, the FP32 contraction
     // Too few 64 x 64 tiles to occupy the GPU: one output per thread instead,
     // so that every SM has chains to run. A batch-64 linear layer of 2048
     // outputs is 32 tiles, which left 116 of 148 SMs idle while each busy
@@ -681,10 +820,25 @@ int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int6
         d.b = B;
         d.c = C;
         d.bias = bias;
+        if (n_launched) *n_launched += 1;
         return launch_contract_staged(p, d, skip, skip ? nullptr : d_route, st);
     }
+    // FP32 and BF16 accumulators: scan both operands for the range proof
+    // (range_proven), on the device, ahead of the two contraction builds.
+    const bool narrow_rm = p->acc != DRIFT_ACC_BF16 || p->acc_rounding == DRIFT_NEAREST_EVEN ||
+                           p->acc_rounding == DRIFT_TRUNCATE;
+    const bool prove = d_scan && (p->acc == DRIFT_ACC_FP32 || p->acc == DRIFT_ACC_BF16) &&
+                       narrow_rm && K > 0 && (double)M * (double)N * (double)K >= kRangeMinMacs &&
+                       range_limit_for(p->acc, K) > -1024;
+    if (prove) {
+        if (cudaMemsetAsync(d_scan, 0, 2 * kRangeWords * sizeof(unsigned), st) != cudaSuccess)
+            return DRIFT_ECUDA;
+        const dim3 sgrid((unsigned)(sm_count() * 4), 2);
+        range_scan_kernel<<<sgrid, 256, 0, st>>>(A, M, a_rs, a_ks, B, N, b_rs, b_ks, K, d_scan);
+        if (n_launched) *n_launched += 1;
+    }
     return gemm_batched(cache, p, 1, M, N, K, A, a_rs, a_ks, 0, B, b_rs, b_ks, 0, bias, C, c_rs, 0,
-                        d_err, skip, st);
+                        d_err, skip, st, prove ? d_scan : nullptr, d_route, n_launched);
 }
 
 int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t batch,
@@ -701,7 +855,8 @@ static int gemm_batched(ScheduleCache &cache, const drift_policy *p, int64_t bat
                         int64_t N, int64_t K, const double *A, int64_t a_rs, int64_t a_ks,
                         int64_t a_bs, const double *B, int64_t b_rs, int64_t b_ks, int64_t b_bs,
                         const double *bias, double *C, int64_t c_rs, int64_t c_bs, int *d_err,
-                        const int *skip, cudaStream_t st) {
+                        const int *skip, cudaStream_t st, const unsigned *range, int *route,
+                        int *n_launched) {
     if (M < 0 || N < 0 || K < 0 || a_rs < 0 || a_ks < 0 || b_rs < 0 || b_ks < 0 || c_rs < 0)
         return DRIFT_EINVAL;
     if (batch < 0 || a_bs < 0 || b_bs < 0 || c_bs < 0 || batch > 65535) return DRIFT_EINVAL;
@@ -758,25 +913,42 @@ static int gemm_batched(ScheduleCache &cache, const drift_policy *p, int64_t bat
         }
     }
     const dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)batch);
+    // With scan words, both builds are queued and the scan picks one; the
+    // proof covers FP32 and BF16 accumulators of one problem.
+    const bool prove = range && batch == 1 &&
+                       (p->acc == DRIFT_ACC_FP32 || p->acc == DRIFT_ACC_BF16);
+    if (prove) {
+        g.range = range;
+        g.range_limit = range_limit_for(p->acc, K);
+        g.route = route;
+    }
     int rc;
+    const bool trunc = p->acc_rounding == DRIFT_TRUNCATE;
     switch (p->acc) {
         case DRIFT_ACC_FP64:
             rc = launch_order<DRIFT_ACC_FP64, DRIFT_NEAREST_EVEN>(p->order, seg, g, ma, mb, grid, st);
             break;
         case DRIFT_ACC_FP32:
             rc = launch_order<DRIFT_ACC_FP32, DRIFT_NEAREST_EVEN>(p->order, seg, g, ma, mb, grid, st);
+            if (!rc && prove)
+                rc = launch_order<DRIFT_ACC_FP32, DRIFT_NEAREST_EVEN, true>(p->order, seg, g, ma, mb,
+                                                                            grid, st);
             break;
         case DRIFT_ACC_FP16:
-            rc = p->acc_rounding == DRIFT_TRUNCATE
-                     ? launch_order<DRIFT_ACC_FP16, DRIFT_TRUNCATE>(p->order, seg, g, ma, mb, grid, st)
-                     : launch_order<DRIFT_ACC_FP16, DRIFT_NEAREST_EVEN>(p->order, seg, g, ma, mb, grid, st);
+            rc = trunc ? launch_order<DRIFT_ACC_FP16, DRIFT_TRUNCATE>(p->order, seg, g, ma, mb, grid, st)
+                       : launch_order<DRIFT_ACC_FP16, DRIFT_NEAREST_EVEN>(p->order, seg, g, ma, mb, grid, st);
             break;
         default:
-            rc = p->acc_rounding == DRIFT_TRUNCATE
-                     ? launch_order<DRIFT_ACC_BF16, DRIFT_TRUNCATE>(p->order, seg, g, ma, mb, grid, st)
-                     : launch_order<DRIFT_ACC_BF16, DRIFT_NEAREST_EVEN>(p->order, seg, g, ma, mb, grid, st);
+            rc = trunc ? launch_order<DRIFT_ACC_BF16, DRIFT_TRUNCATE>(p->order, seg, g, ma, mb, grid, st)
+                       : launch_order<DRIFT_ACC_BF16, DRIFT_NEAREST_EVEN>(p->order, seg, g, ma, mb, grid, st);
+            if (!rc && prove)
+                rc = trunc ? launch_order<DRIFT_ACC_BF16, DRIFT_TRUNCATE, true>(p->order, seg, g, ma,
+                                                                                mb, grid, st)
+                           : launch_order<DRIFT_ACC_BF16, DRIFT_NEAREST_EVEN, true>(p->order, seg, g,
+                                                                                    ma, mb, grid, st);
     }
     if (rc) return rc;
+    if (n_launched) *n_launched += prove ? 2 : 1;
     return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 

@@ -109,13 +109,17 @@ int launch_gemm_batched(Workspace &ws, ScheduleCache &cache, const drift_policy 
 int launch_fp64_probe(cudaStream_t st, double *ops_per_s);
 int launch_fp32_probe(cudaStream_t st, double *fma_per_s);
 // One contraction C = A B^T (+ bias). `d_route`, when given, receives the
-// DRIFT_ROUTE_* of the path taken.
+// DRIFT_ROUTE_* of the path taken. `d_scan` (8 device words), when given,
+// lets FP32 and BF16 accumulators scan their operands for the range proof
+// that drops the per-step checks. `*n_launched` receives the number of
+// kernels queued.
 // Calls with fewer 64 x 64 output tiles than `thin_tiles` run one output per
 // thread (launch_contract_staged); a negative value means two per SM.
 int launch_gemm(Workspace &ws, ScheduleCache &cache, const drift_policy *p, int64_t M, int64_t N,
                 int64_t K, const double *A, int64_t a_rs, int64_t a_ks, const double *B,
                 int64_t b_rs, int64_t b_ks, const double *bias, double *C, int64_t c_rs,
-                int64_t thin_tiles, int *d_err, int *d_route, cudaStream_t st);
+                int64_t thin_tiles, int *d_err, int *d_route, cudaStream_t st,
+                unsigned *d_scan = nullptr, int *n_launched = nullptr);
 // gemm32.cu: queues the FP32-pipe path of an FP32-accumulated contraction
 // whose policy and shape qualify (an operand scan, a device-side decision and
 // the FFMA contraction, which stands down unless the scan allows it). Sets

@@ -403,7 +403,7 @@ def error_sums_dev(got, exact, d_sums, *, stream=None, ctx=None) -> None:
                                                 got.numel(), _tptr(d_sums), _stream_ptr(stream)))
 
 
-ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED, ROUTE_STAGED = 0, 1, 2, 3
+ROUTE_DOUBLE, ROUTE_FP32, ROUTE_SCANNED, ROUTE_STAGED, ROUTE_PROVEN = 0, 1, 2, 3, 4
 
 
 def gemm_route(stream=None, ctx=None) -> int:
@@ -411,11 +411,22 @@ def gemm_route(stream=None, ctx=None) -> int:
     FP32 pipe (narrow products under an FP32 accumulator), ROUTE_SCANNED for a
     candidate whose operands kept it on the double-precision contraction,
     ROUTE_STAGED for one output per thread (a call too thin to fill the GPU
-    with 64 x 64 tiles), ROUTE_DOUBLE for the tiled double-precision
+    with 64 x 64 tiles), ROUTE_PROVEN for the double-precision contraction
+    of an FP32/BF16 accumulator whose operand scan proved every partial sum in
+    range (no per-step checks), ROUTE_DOUBLE for the tiled double-precision
     contraction alone. Synchronises the stream."""
     ctx = ctx or _lib.Context.current()
     out = ctypes.c_int()
     _lib.check(_lib.load().drift_gemm_route(ctx.handle, ctypes.byref(out), _stream_ptr(stream)))
+    return out.value
+
+
+def gemm_launches(ctx=None) -> int:
+    """How many kernels the context's last non-stochastic GEMM call queued
+    (scans, decisions and both builds of a scanned route included)."""
+    ctx = ctx or _lib.Context.current()
+    out = ctypes.c_int()
+    _lib.check(_lib.load().drift_gemm_launches(ctx.handle, ctypes.byref(out)))
     return out.value
 
 

@@ -330,15 +330,29 @@ DRIFT_API int drift_gemm_dev(drift_ctx *ctx, const drift_policy *p, int64_t M,
  *                          kept it on the double-precision contraction;
  *   DRIFT_ROUTE_STAGED   3  one output per thread with the operands staged in
  *                          shared memory (one launch): a call too thin for
- *                          the tiled kernel (drift_set_thin_tiles).
- * Every route gives the same bits; the route is a performance fact (routes 1
- * and 2 launch five kernels: two scans, the decision and both contractions,
- * one of which stands down). Waits for `stream`. */
+ *                          the tiled kernel (drift_set_thin_tiles);
+ *   DRIFT_ROUTE_PROVEN   4  the double-precision contraction of an FP32 or
+ *                          BF16 accumulator without its per-step range
+ *                          checks: a scan of both operands proved that every
+ *                          partial sum stays in the accumulator's normal range
+ *                          below its top binade (nonzero |a|·|b| >= 2^-74, no
+ *                          Inf, NaN or subnormal, and the largest magnitudes
+ *                          bound K sums below 2^126).
+ * Every route gives the same bits; the route is a performance fact.
+ * Waits for `stream`. */
 #define DRIFT_ROUTE_DOUBLE 0
 #define DRIFT_ROUTE_FP32 1
 #define DRIFT_ROUTE_SCANNED 2
 #define DRIFT_ROUTE_STAGED 3
+#define DRIFT_ROUTE_PROVEN 4
 DRIFT_API int drift_gemm_route(drift_ctx *ctx, int *route, void *stream);
+
+/* No counterpart in the reference (a performance fact): the number of kernels
+ * the context's most recent drift_gemm_dev (or the last chunk of a drift_gemm)
+ * with a non-stochastic accumulator queued: the contraction, plus the
+ * operand scans, decisions and second contraction builds of the FP32-pipe and
+ * range-proof routes (the build the scan does not pick leaves at once). */
+DRIFT_API int drift_gemm_launches(drift_ctx *ctx, int *launches);
 
 /* No counterpart in the reference (a tuning knob; results do not change):
  * drift_gemm / drift_gemm_dev calls whose M x N outputs make fewer than

@@ -91,3 +91,46 @@ class OracleBackend:
         if rng is not None:
             rng.reseed(st)
         return C
+
+
+def range_limit(bf16: bool, K: int) -> int:
+    """The contraction's range-proof bound on ta + tb + 2 for K terms
+    (range_limit_for in gemm.cu): 126 - ceil(log2 K) - ceil(log2 (1+d)^(K+1)),
+    d the relative error of a double add then the accumulator's rounding."""
+    u = 2.0 ** -8 if bf16 else 2.0 ** -24
+    d = u + 2.0 ** -53 + u * 2.0 ** -53
+    growth = (K + 1) * np.log1p(d) / np.log(2.0)
+    lg = int(np.ceil(np.log2(K))) if K > 1 else 0
+    return 126 - lg - int(np.ceil(growth + 1e-9))
+
+
+def range_proven(bf16: bool, a, b, K: int) -> bool:
+    """Whether the contraction's operand scan proves every partial sum of an
+    FP32 (or BF16) accumulator in range (range_proven in gemm.cu): no Inf,
+    NaN or subnormal; the smallest nonzero magnitudes' binade exponents sum to
+    at least -74; the largest ones' plus 2 to at most range_limit."""
+    ex = []
+    for x in (a, b):
+        x = np.abs(np.asarray(x, dtype=np.float64).reshape(-1))
+        if np.isnan(x).any() or np.isinf(x).any():
+            return False
+        x = x[x != 0]
+        if x.size == 0:
+            return True
+        if (x < 2.0 ** -1022).any():
+            return False
+        e = np.frexp(x)[1] - 1                  # |x| in [2^e, 2^(e+1))
+        ex.append((int(e.min()), int(e.max())))
+    (la, ta), (lb, tb) = ex
+    return la + lb >= -74 and ta + tb + 2 <= range_limit(bf16, K)
+
+
+def tiled_route(acc: int, M: int, N: int, K: int, a, b, rounding: int = 0) -> int:
+    """The route a tiled (not thin, not FP32-pipe) non-stochastic GEMM
+    reports: 4 (range proven, no per-step checks) for an FP32 or BF16
+    accumulator over at least 2^27 multiply-accumulates whose operands pass
+    the proof, else 0."""
+    if acc in (1, 3) and rounding in (0, 2) and K > 0 and M * N * K >= 1 << 27:
+        if range_proven(acc == 3, a, b, K):
+            return 4
+    return 0

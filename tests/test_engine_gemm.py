@@ -125,14 +125,16 @@ def test_pairwise_trees_regular_and_irregular(d, acc, K):
     compare(d, acc, 2, 0, M, N, K, A, 0, K, 1, B, 0, K, 1)
 
 
-@pytest.mark.parametrize("acc", ACCS)
+@pytest.mark.parametrize("acc,rm", [(a, r) for a in ACCS for r in ([0, 2] if a >= 2 else [0])])
 @pytest.mark.parametrize("acc_block", [1, 7, 32, 37, 64, 96, 1000])
-def test_blocked_any_chunk(d, acc, acc_block):
+def test_blocked_any_chunk(d, acc, rm, acc_block):
+    """Chunks on and off the 16-wide k tile, both accumulator roundings; 70
+    columns cover every column slot of a thread's 4 x 4 block."""
     rs = np.random.default_rng(acc_block)
     M, N, K = 5, 70, 300
     A = heavy_tailed(rs, M * K)
     B = heavy_tailed(rs, N * K)
-    compare(d, acc, 3, 0, M, N, K, A, 0, K, 1, B, 0, K, 1, acc_block=acc_block)
+    compare(d, acc, 3, rm, M, N, K, A, 0, K, 1, B, 0, K, 1, acc_block=acc_block)
 
 
 def test_summation_order_changes_fp32_answer(d):

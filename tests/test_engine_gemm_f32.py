@@ -14,7 +14,7 @@ too thin for the tiles). Bit-exact against the oracle either way."""
 import numpy as np
 import pytest
 
-from helpers import assert_bits, heavy_tailed
+from helpers import assert_bits, heavy_tailed, tiled_route
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -165,7 +165,9 @@ def test_ineligible_operands_stay_exact(d, case):
         A, _, _ = O.quantize(O.policy(input_format=f, scaling=1), f, 0, x, sa)
     else:
         A = heavy_tailed(rs, M * K)
-    check(d, SEQ, M, N, K, A, K, 1, B, K, 1, route=2)   # scanned, stayed
+    # Scanned, stayed on the double-precision contraction (route 2): a call of
+    # 64 tiles, which runs one output per thread.
+    check(d, SEQ, M, N, K, A, K, 1, B, K, 1, route=2)
 
 
 def test_pairwise_and_small_stay_on_double_path(d):
@@ -173,17 +175,19 @@ def test_pairwise_and_small_stay_on_double_path(d):
     A = bf16_cast(heavy_tailed(rs, 512 * 512))
     B = bf16_cast(heavy_tailed(rs, 512 * 512))
     # Forced to one output per thread (route 3), then to the tiled kernel.
-    for thin, r in ((1 << 40, 3), (0, 0)):
+    # Tiled calls of at least 2^27 MACs take the range proof (route 4).
+    big = tiled_route(1, 512, 512, 512, A, B)
+    for thin, r, rbig in ((1 << 40, 3, 3), (0, 0, big)):
         d.set_thin_tiles(thin)
         try:
-            check(d, PAIR, 512, 512, 512, A, 512, 1, B, 512, 1, route=r)
+            check(d, PAIR, 512, 512, 512, A, 512, 1, B, 512, 1, route=rbig)
             check(d, SEQ, 256, 256, 256, A, 256, 1, B, 256, 1, route=r)  # below 2^27 MACs
-            check(d, BLOCK, 512, 512, 512, A, 512, 1, B, 512, 1, route=r, blk=40)  # chunk off-tile
+            check(d, BLOCK, 512, 512, 512, A, 512, 1, B, 512, 1, route=rbig, blk=40)  # off-tile
         finally:
             d.set_thin_tiles(-1)
     # By default pairwise over 512 x 512 outputs (64 tiles of 64 x 64) stays
     # tiled, and sequential over 256 x 256 (16 tiles) goes one output per thread.
-    check(d, PAIR, 512, 512, 512, A, 512, 1, B, 512, 1, route=0)
+    check(d, PAIR, 512, 512, 512, A, 512, 1, B, 512, 1, route=big)
     check(d, SEQ, 256, 256, 256, A, 256, 1, B, 256, 1, route=3)
 
 

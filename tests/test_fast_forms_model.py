@@ -19,6 +19,7 @@ is an exact product plus one rounded add, so numpy's float64 add restates it.
 import numpy as np
 import pytest
 
+from helpers import range_limit, range_proven
 from oracle import oracle as O
 
 
@@ -200,3 +201,96 @@ def test_bit_pattern_stochastic_rounding_matches_oracle(acc):
         assert s2 == w2, v
         state = s2
     assert taken > n // 2
+
+
+# ------------------------------------------------------------------ range proof
+
+def _range_limit(acc, K):
+    return range_limit(acc == O.ACC_BF16, K)
+
+
+def _range_proven(acc, a, b, K):
+    return range_proven(acc == O.ACC_BF16, a, b, K)
+
+
+def _proven_operands(rs, n, k, lo, hi, cancel=True):
+    """n rows of k terms, nonzero magnitudes in [2^lo, 2^hi), a tenth zeros.
+    With `cancel`, every odd term of half the rows repeats its even
+    neighbour's product negated, so those partial sums fall back to rounding
+    residues again and again (the low side's worst case)."""
+    def draw():
+        e = rs.integers(lo, hi, (n, k))
+        return np.ldexp(1.0 + rs.random((n, k)), e) * np.where(rs.random((n, k)) < 0.5, -1.0, 1.0)
+    a, b = draw(), draw()
+    if cancel:
+        h = n // 2
+        a[:h, 1::2] = a[:h, 0::2]
+        b[:h, 1::2] = -b[:h, 0::2]
+    a[rs.random((n, k)) < 0.05] = 0.0
+    b[rs.random((n, k)) < 0.05] = 0.0
+    return a, b
+
+
+def _fast_chain_step(acc_id, t, prev_lo):
+    shift = 29 if acc_id == O.ACC_FP32 else 45
+    return _fast_round(t, prev_lo, shift, 1023 - 126, 1023 + 126)
+
+
+def _lo_word(x):
+    return (x.view(np.uint64) & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+
+
+@pytest.mark.parametrize("acc", [O.ACC_FP32, O.ACC_BF16])
+@pytest.mark.parametrize("case", ["low", "high"])
+def test_range_proof_keeps_every_sum_exact(acc, case):
+    """Under the range proof's bounds, the unchecked fast rounding equals
+    Dot.round at every step of sequential chains and of pairwise trees
+    (leaves of 8, Dot.java:86-102): every sum is in the fast form's range or
+    is +0, which the fast form also returns."""
+    rs = np.random.default_rng(77 + acc + (case == "high"))
+    K = 512
+    lo, hi = (-37, 8) if case == "low" else (40, 56)
+    a, b = _proven_operands(rs, 600, K, lo, hi, cancel=case == "low")
+    if case == "high":
+        b = np.abs(b) * np.sign(a + (a == 0))       # every product >= 0: sums grow
+    assert _range_proven(acc, a, b, K)
+    prods = a * b
+
+    def check_round(t, prev_lo):
+        got, valid = _fast_chain_step(acc, t, prev_lo)
+        if acc == O.ACC_FP32:
+            want = t.astype(np.float32).astype(np.float64)     # Java's (float)
+        else:
+            want = O.acc_round(acc, O.NEAREST_EVEN, t)[0]
+        assert (got.view(np.int64) == want.view(np.int64)).all()
+        plus_zero = t.view(np.int64) == 0
+        assert (valid | plus_zero).all()
+        return want
+
+    # Sequential (Dot.java:50-56).
+    s = np.zeros(prods.shape[0])
+    for j in range(K):
+        s = check_round(s + prods[:, j], _lo_word(s))
+    # Pairwise over 8-term leaves, combined as a perfect tree.
+    leaves = []
+    for l0 in range(0, K, 8):
+        s = np.zeros(prods.shape[0])
+        for j in range(l0, l0 + 8):
+            s = check_round(s + prods[:, j], _lo_word(s))
+        leaves.append(s)
+    while len(leaves) > 1:
+        leaves = [check_round(leaves[i] + leaves[i + 1], _lo_word(leaves[i + 1]))
+                  for i in range(0, len(leaves), 2)]
+
+
+def test_range_proof_rejects_out_of_bound_operands():
+    rs = np.random.default_rng(3)
+    a, b = _proven_operands(rs, 8, 64, -20, 4)
+    assert _range_proven(O.ACC_FP32, a, b, 64)
+    for bad in (2.0 ** -60, np.inf, np.nan, 5e-324, 2.0 ** 120):
+        a2 = a.copy()
+        a2[3, 5] = bad
+        assert not _range_proven(O.ACC_FP32, a2, b, 64), bad
+    # BF16's growth term: (1 + 2^-8)^(K+1) takes 47 bits at K = 8192.
+    assert _range_limit(O.ACC_BF16, 8192) == 126 - 13 - 47
+    assert _range_limit(O.ACC_FP32, 8192) == 126 - 13 - 1
