@@ -301,6 +301,18 @@ struct FastForm {
         range = exp_word(t) - kBase;
         return __hiloint2double(__double2hiint(t) & ~((1 << (SHIFT - 32)) - 1), 0);
     }
+    // Round to nearest even on the integer pipes: add half a quantum less one
+    // plus the kept part's lowest bit to t's bit pattern, then clear the
+    // dropped bits (a carry out of the significand moves t into the next
+    // binade, as rounding up should). Exact on the same range as rne. It
+    // takes no FP64 instruction, so a contraction that rounds some of its
+    // sums this way and the rest with rne keeps both pipes busy.
+    __device__ static __forceinline__ double rne_int(double t, unsigned &range) {
+        range = exp_word(t) - kBase;
+        unsigned long long u = (unsigned long long)__double_as_longlong(t);
+        u += ((1ULL << (SHIFT - 1)) - 1) + ((u >> SHIFT) & 1ULL);
+        return __longlong_as_double((long long)(u & ~((1ULL << SHIFT) - 1)));
+    }
     // Folds two range words into a group's running max.
     __device__ static __forceinline__ unsigned fold2(unsigned run, unsigned r0, unsigned r1) {
         return __vimax3_u32(run, r0, r1);
@@ -312,6 +324,7 @@ struct FastForm {
 //   step(t, prev_lo, r)    the fast form above (prev_lo: the low word of the
 //                          accumulator value this sum replaces, or 0; r gets
 //                          the sum's range word);
+//   step_int(t, r)         the same rounding on the integer pipes;
 //   fold2(run, r0, r1)     folds two range words into a group's word;
 //   valid(run)             whether every step folded into run was exact;
 //   fast(t) / ok(r)        the older rne_shift form with a range check on the
@@ -321,6 +334,7 @@ template <int ACC, int RM> struct AccRound;
 
 template <int RM> struct AccRound<DRIFT_ACC_FP64, RM> {
     __device__ static double step(double t, int, unsigned &) { return t; }
+    __device__ static double step_int(double t, unsigned &) { return t; }
     __device__ static unsigned fold2(unsigned run, unsigned, unsigned) { return run; }
     __device__ static bool valid(unsigned) { return true; }
     __device__ static double fast(double t) { return t; }
@@ -334,6 +348,7 @@ template <int RM> struct AccRound<DRIFT_ACC_FP32, RM> {
     __device__ static double step(double t, int prev_lo, unsigned &run) {
         return Fast::rne(t, prev_lo, run);
     }
+    __device__ static double step_int(double t, unsigned &run) { return Fast::rne_int(t, run); }
     __device__ static unsigned fold2(unsigned run, unsigned r0, unsigned r1) {
         return Fast::fold2(run, r0, r1);
     }
@@ -372,6 +387,9 @@ template <int RM> struct AccRound<DRIFT_ACC_FP16, RM> {
     __device__ static double step(double t, int prev_lo, unsigned &run) {
         return RM == DRIFT_TRUNCATE ? Fast::trunc(t, prev_lo, run) : Fast::rne(t, prev_lo, run);
     }
+    __device__ static double step_int(double t, unsigned &run) {
+        return RM == DRIFT_TRUNCATE ? Fast::trunc(t, 0, run) : Fast::rne_int(t, run);
+    }
     __device__ static unsigned fold2(unsigned run, unsigned r0, unsigned r1) {
         return Fast::fold2(run, r0, r1);
     }
@@ -390,6 +408,9 @@ template <int RM> struct AccRound<DRIFT_ACC_BF16, RM> {
     using Fast = FastForm<52 - F::mant, 1023 + F::min_exp, 1023 + F::max_exp - 1>;
     __device__ static double step(double t, int prev_lo, unsigned &run) {
         return RM == DRIFT_TRUNCATE ? Fast::trunc(t, prev_lo, run) : Fast::rne(t, prev_lo, run);
+    }
+    __device__ static double step_int(double t, unsigned &run) {
+        return RM == DRIFT_TRUNCATE ? Fast::trunc(t, 0, run) : Fast::rne_int(t, run);
     }
     __device__ static unsigned fold2(unsigned run, unsigned r0, unsigned r1) {
         return Fast::fold2(run, r0, r1);

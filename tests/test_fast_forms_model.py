@@ -294,3 +294,38 @@ def test_range_proof_rejects_out_of_bound_operands():
     # BF16's growth term: (1 + 2^-8)^(K+1) takes 47 bits at K = 8192.
     assert _range_limit(O.ACC_BF16, 8192) == 126 - 13 - 47
     assert _range_limit(O.ACC_FP32, 8192) == 126 - 13 - 1
+
+
+def _int_round(t, shift):
+    """FastForm.rne_int (codec.cuh) on t's bit pattern: add half a quantum
+    less one plus the kept part's lowest bit, clear the dropped bits."""
+    u = t.view(np.uint64).copy()
+    s = np.uint64(shift)
+    u += (np.uint64(1) << (s - np.uint64(1))) - np.uint64(1) + ((u >> s) & np.uint64(1))
+    u &= ~((np.uint64(1) << s) - np.uint64(1))
+    return u.view(np.float64)
+
+
+@pytest.mark.parametrize("acc", ["fp32", "fp16", "bf16"])
+def test_integer_pipe_rounding_matches_oracle(acc):
+    """The integer-pipe form of round-to-nearest-even agrees with Dot.round /
+    (float) on every sum the range word admits, ties included."""
+    rs = np.random.default_rng(21)
+    n = 600_000
+    if acc == "fp32":
+        shift, lo_e, hi_e = 29, 1023 - 126, 1023 + 126
+        t = _sums(rs, n, shift, -150, 130)
+        with np.errstate(over="ignore"):
+            want = t.astype(np.float32).astype(np.float64)
+    else:
+        acc_id = 2 if acc == "fp16" else 3
+        mant, min_e, max_e = (10, -14, 15) if acc == "fp16" else (7, -126, 127)
+        shift, lo_e, hi_e = 52 - mant, 1023 + min_e, 1023 + max_e - 1
+        t = _sums(rs, n, shift, min_e - 10, max_e + 3)
+        want = O.acc_round(acc_id, O.NEAREST_EVEN, t)[0]
+    _, valid = _fast_round(t, np.zeros(n, np.uint32), shift, lo_e, hi_e)
+    with np.errstate(all="ignore"):
+        got = _int_round(t, shift)
+    bad = valid & (got.view(np.int64) != want.view(np.int64))
+    assert not bad.any(), (acc, t[bad][:3])
+    assert valid.mean() > 0.6
