@@ -7,6 +7,8 @@
 // random draw, then fetch exactly that draw from the counter-based stream.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace drift {
@@ -349,6 +351,8 @@ template <int RM> struct AccRound<DRIFT_ACC_FP32, RM> {
         return Fast::rne(t, prev_lo, run);
     }
     __device__ static double step_int(double t, unsigned &run) { return Fast::rne_int(t, run); }
+    // On the conversion pipe: cvt.rn.f32.f64 and back, (float) itself.
+    __device__ static double step_cvt(double t) { return (double)__double2float_rn(t); }
     __device__ static unsigned fold2(unsigned run, unsigned r0, unsigned r1) {
         return Fast::fold2(run, r0, r1);
     }
@@ -411,6 +415,12 @@ template <int RM> struct AccRound<DRIFT_ACC_BF16, RM> {
     }
     __device__ static double step_int(double t, unsigned &run) {
         return RM == DRIFT_TRUNCATE ? Fast::trunc(t, 0, run) : Fast::rne_int(t, run);
+    }
+    // On the conversion pipe: cvt.rn.bf16.f64 and back. Nearest even with
+    // subnormals, as Dot.round; it gives Inf where Dot.round saturates, so it
+    // serves only sums proven to stay below the top binade.
+    __device__ static double step_cvt(double t) {
+        return (double)__bfloat162float(__double2bfloat16(t));
     }
     __device__ static unsigned fold2(unsigned run, unsigned r0, unsigned r1) {
         return Fast::fold2(run, r0, r1);

@@ -94,19 +94,28 @@ constexpr int kp_unroll() {
 
 enum SegMode { SEG_NONE = 0, SEG_TILE = 1, SEG_SCHED = 2 };
 
-// How many of a thread's four output columns round on the integer pipes
-// (step_int) instead of the FP64 pipe (step): splitting the rounding between
-// the two pipes lifts the FP64 pipe's share below four operations per MAC.
-// Measured at 8192^3 on one B200 (range-proven builds; one column / two):
-// FP32 sequential +5.1% / +6.3%, pairwise +5.4% / +4.2%, blocked +4.2% /
-// +4.8%; BF16 sequential +2.5% / +5.0%, pairwise +3.0% / +2.0%, blocked
-// +3.0% / -0.3%.
+// The proven FP32/BF16 builds round a thread's four output columns on three
+// pipes: the last column on the conversion pipe (cvt to float / bf16 and
+// back, step_cvt), the int_cols columns before it on the integer pipes
+// (step_int), the rest on the FP64 pipe (step). Splitting the rounding lifts
+// the FP64 pipe's share below four operations per MAC. Measured at 8192^3 on
+// one B200, one integer column and the conversion column against every
+// column on the FP64 pipe: FP32 sequential +8.6%, pairwise +5.3%, blocked
+// +7.7%; BF16 sequential +7.9%, pairwise +5.2%, blocked +5.7%; two integer
+// columns: FP32 sequential and blocked another +1.9% and +1.0%, BF16
+// sequential and blocked -2.6% and -3.4%. (The
+// conversion column alone: FP32 pairwise +3.2%, BF16 pairwise +2.7%,
+// blocked +1.0%; integer columns alone, one / two: FP32 sequential +5.1% /
+// +6.3%, BF16 sequential +2.5% / +5.0%. Two conversion columns saturate that
+// pipe: FP32 sequential +0.6%.)
+template <int ACC, int RM, bool PROVEN>
+constexpr bool cvt_col() {
+    return PROVEN && RM == DRIFT_NEAREST_EVEN && (ACC == DRIFT_ACC_FP32 || ACC == DRIFT_ACC_BF16);
+}
 template <int ACC, int ORDER, int RM, bool PROVEN>
 constexpr int int_cols() {
-    if (!PROVEN || RM != DRIFT_NEAREST_EVEN) return 0;
-    if (ACC == DRIFT_ACC_FP32) return ORDER == DRIFT_PAIRWISE ? 1 : 2;
-    if (ACC == DRIFT_ACC_BF16) return ORDER == DRIFT_SEQUENTIAL || ORDER == DRIFT_REVERSED ? 2 : 1;
-    return 0;
+    if (!cvt_col<ACC, RM, PROVEN>()) return 0;
+    return ACC == DRIFT_ACC_FP32 && ORDER != DRIFT_PAIRWISE ? 2 : 1;
 }
 
 // The accumulator rounding of a contraction. PROVEN: an operand scan showed
@@ -174,6 +183,7 @@ template <int ACC, int RM, int G = GROUP_ROWS, bool FIRST = false, bool PV = fal
 __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[TM],
                                       const double (&b)[TN]) {
     using R = GemmRound<ACC, RM, PV>;
+    constexpr int CV = cvt_col<ACC, RM, PV>() ? 1 : 0;
     if constexpr (ACC == DRIFT_ACC_FP64) {
 #pragma unroll
         for (int i = 0; i < TM; i++)
@@ -190,8 +200,15 @@ __device__ __forceinline__ void mac16(double (&acc)[TM][TN], const double (&a)[T
 #pragma unroll
                 for (int j = 0; j < TN; j++) {
                     t[i][j] = __dadd_rn(FIRST ? 0.0 : acc[i0 + i][j], __dmul_rn(a[i0 + i], b[j]));
+                    if constexpr (CV == 1) {
+                        if (j == TN - 1) {
+                            acc[i0 + i][j] = R::step_cvt(t[i][j]);
+                            u[i][j] = 0;
+                            continue;
+                        }
+                    }
                     acc[i0 + i][j] =
-                        j >= TN - NI
+                        j >= TN - CV - NI
                             ? R::step_int(t[i][j], u[i][j])
                             : R::step(t[i][j], FIRST ? 0 : __double2loint(acc[i0 + i][j]), u[i][j]);
                 }
@@ -216,14 +233,22 @@ template <int ACC, int RM, bool FIRST = false, bool PV = false, int NI = 0>
 __device__ __forceinline__ void mac16_run(double (&acc)[TM][TN], const double (&a)[TM],
                                           const double (&b)[TN], unsigned &run) {
     using R = GemmRound<ACC, RM, PV>;
+    constexpr int CV = cvt_col<ACC, RM, PV>() ? 1 : 0;
 #pragma unroll
     for (int i = 0; i < TM; i++) {
         unsigned u[TN];
 #pragma unroll
         for (int j = 0; j < TN; j++) {
             const double t = __dadd_rn(FIRST ? 0.0 : acc[i][j], __dmul_rn(a[i], b[j]));
-            acc[i][j] = j >= TN - NI ? R::step_int(t, u[j])
-                                     : R::step(t, FIRST ? 0 : __double2loint(acc[i][j]), u[j]);
+            if constexpr (CV == 1) {
+                if (j == TN - 1) {
+                    acc[i][j] = R::step_cvt(t);
+                    u[j] = 0;
+                    continue;
+                }
+            }
+            acc[i][j] = j >= TN - CV - NI ? R::step_int(t, u[j])
+                                          : R::step(t, FIRST ? 0 : __double2loint(acc[i][j]), u[j]);
         }
 #pragma unroll
         for (int j = 0; j < TN; j += 2) run = R::fold2(run, u[j], u[j + 1]);
