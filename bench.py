@@ -42,7 +42,7 @@ METRIC = "bit-exact emulated MAC/s per policy at 1/2/4/8 B200 vs Java host; mism
 # same kernels at 4096^3 (dram__bytes_read.sum + dram__bytes_write.sum per
 # launch over its MACs); a launch's traffic scales with its MAC count because
 # every operand tile is re-read once per 64-wide output tile.
-DRAM_BYTES_PER_MAC = {"pairwise": 0.150, "other": 0.0583}
+DRAM_BYTES_PER_MAC = {"pairwise": 0.144, "other": 0.0583}
 UNIT = "emulated MAC/s"
 # The sweep's policies by name, in order (sweep_policies builds them for the
 # engine; the reference arm, which loads no engine code, names them here).
