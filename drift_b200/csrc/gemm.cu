@@ -297,6 +297,8 @@ __device__ __forceinline__ void blocked_fold(double (&tot)[TM][TN], double (&acc
 template <int ACC, int RM, bool PV = false>
 __device__ __forceinline__ void combine(const double (&left)[TM][TN], double (&right)[TM][TN]) {
     using R = GemmRound<ACC, RM, PV>;
+    constexpr int CV = cvt_col<ACC, RM, PV>() ? 1 : 0;
+    constexpr int NI = int_cols<ACC, DRIFT_PAIRWISE, RM, PV>();
 #pragma unroll
     for (int i0 = 0; i0 < TM; i0 += GROUP_ROWS) {
         double t[GROUP_ROWS][TN];
@@ -306,7 +308,16 @@ __device__ __forceinline__ void combine(const double (&left)[TM][TN], double (&r
 #pragma unroll
             for (int j = 0; j < TN; j++) {
                 t[i][j] = __dadd_rn(left[i0 + i][j], right[i0 + i][j]);
-                right[i0 + i][j] = R::step(t[i][j], __double2loint(right[i0 + i][j]), u[i][j]);
+                if constexpr (CV == 1) {
+                    if (j == TN - 1) {
+                        right[i0 + i][j] = R::step_cvt(t[i][j]);
+                        u[i][j] = 0;
+                        continue;
+                    }
+                }
+                right[i0 + i][j] = j >= TN - CV - NI
+                                       ? R::step_int(t[i][j], u[i][j])
+                                       : R::step(t[i][j], __double2loint(right[i0 + i][j]), u[i][j]);
             }
 #pragma unroll
         for (int i = 0; i < GROUP_ROWS; i++)
