@@ -79,6 +79,11 @@ __host__ __device__ inline int radix_shift(int pass) {
     return s < 0 ? 0 : s;
 }
 
+// The first passes' digits are the top bits of the errors' bit patterns,
+// which most elements share (errors of one policy span a few binades), so the
+// lanes of a warp that hold the same digit add it once (match_any); the later
+// passes count the few elements still matching the prefix, spread over many
+// bins, directly. The loop is warp-uniform so that every lane takes part.
 __global__ void __launch_bounds__(256) radix_hist_kernel(const double *got, const double *exact,
                                                          int64_t n, int pass,
                                                          const unsigned long long *state,
@@ -90,11 +95,23 @@ __global__ void __launch_bounds__(256) radix_hist_kernel(const double *got, cons
     const int top = 64 - kRadixBits * pass;  // bits >= top are already chosen
     const uint64_t prefix = state[0];
     const uint64_t mask = (uint64_t)((1u << (top - shift)) - 1u);
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const uint64_t key = rel_error_key(got[i], exact[i]);
-        if (top == 64 || (key >> top) == (prefix >> top))
-            atomicAdd(&s_hist[(key >> shift) & mask], 1u);
+    const bool aggregate = pass < 2;
+    const int lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < n; base += stride) {
+        const int64_t i = base + threadIdx.x;
+        unsigned bin = 0xFFFFFFFFu;  // not counted
+        if (i < n) {
+            const uint64_t key = rel_error_key(got[i], exact[i]);
+            if (top == 64 || (key >> top) == (prefix >> top)) bin = (unsigned)((key >> shift) & mask);
+        }
+        if (aggregate) {
+            const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
+            if (bin != 0xFFFFFFFFu && lane == __ffs(peers) - 1)
+                atomicAdd(&s_hist[bin], (unsigned)__popc(peers));
+        } else if (bin != 0xFFFFFFFFu) {
+            atomicAdd(&s_hist[bin], 1u);
+        }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < kRadixBins; i += blockDim.x)
@@ -102,21 +119,56 @@ __global__ void __launch_bounds__(256) radix_hist_kernel(const double *got, cons
 }
 
 // state[0] = digits chosen so far, state[1] = rank still sought among the
-// elements that match them. One thread scans the bins in order.
-__global__ void radix_select_kernel(int pass, const unsigned long long *hist,
-                                    unsigned long long *state) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+// elements that match them. One CTA of 256 threads: thread t sums bins
+// [8t, 8t+8), a block-wide exclusive scan of those sums finds the thread
+// whose bins hold rank k, and that thread picks the bin.
+constexpr int kSelectThreads = 256;
+__global__ void __launch_bounds__(kSelectThreads) radix_select_kernel(int pass,
+                                                                      const unsigned long long *hist,
+                                                                      unsigned long long *state) {
+    constexpr int kPer = kRadixBins / kSelectThreads;
+    __shared__ unsigned long long warp_sum[kSelectThreads / 32];
     const int shift = radix_shift(pass);
-    const int width = 64 - kRadixBits * pass - shift;
-    unsigned long long k = state[1];
-    int bin = 0;
-    for (; bin < (1 << width); bin++) {
-        if (k < hist[bin]) break;
-        k -= hist[bin];
+    const int bins = 1 << (64 - kRadixBits * pass - shift);
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const unsigned long long k = state[1];
+    unsigned long long h[kPer], mine = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; j++) {
+        const int b = t * kPer + j;
+        h[j] = b < bins ? hist[b] : 0ULL;
+        mine += h[j];
     }
-    if (bin == (1 << width)) bin = (1 << width) - 1;  // k out of range: stay at the top
-    state[0] |= (unsigned long long)bin << shift;
-    state[1] = k;
+    // Inclusive scan of the per-thread sums within the warp, then across warps.
+    unsigned long long incl = mine;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const unsigned long long v = __shfl_up_sync(0xFFFFFFFFu, incl, d);
+        if (lane >= d) incl += v;
+    }
+    if (lane == 31) warp_sum[warp] = incl;
+    __syncthreads();
+    unsigned long long before = incl - mine;
+    for (int w = 0; w < warp; w++) before += warp_sum[w];
+    unsigned long long total = 0;
+    for (int w = 0; w < kSelectThreads / 32; w++) total += warp_sum[w];
+    __syncthreads();
+    // The thread whose range holds rank k picks the bin; if k is out of
+    // range (never, for a valid k), the last thread stays at the top bin.
+    const bool holds = k >= before && k < before + mine;
+    const bool last = t == kSelectThreads - 1 && k >= total;
+    if (holds || last) {
+        unsigned long long r = k - before;
+        int j = 0;
+        for (; j < kPer; j++) {
+            if (r < h[j]) break;
+            r -= h[j];
+        }
+        int bin = t * kPer + (j < kPer ? j : kPer - 1);
+        if (bin >= bins) bin = bins - 1;
+        state[0] |= (unsigned long long)bin << shift;
+        state[1] = r;
+    }
 }
 
 int launch_radix_pass(const double *got, const double *exact, int64_t n, int pass,
@@ -136,7 +188,7 @@ int launch_radix_pass(const double *got, const double *exact, int64_t n, int pas
 int launch_radix_select(int pass, const unsigned long long *hist, unsigned long long *state,
                         cudaStream_t st) {
     if (pass < 0 || pass >= kRadixPasses) return DRIFT_EINVAL;
-    radix_select_kernel<<<1, 32, 0, st>>>(pass, hist, state);
+    radix_select_kernel<<<1, kSelectThreads, 0, st>>>(pass, hist, state);
     return cudaGetLastError() == cudaSuccess ? DRIFT_OK : DRIFT_ECUDA;
 }
 

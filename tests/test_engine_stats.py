@@ -39,6 +39,16 @@ def test_kth_relative_error_matches_sort():
         assert (np.isnan(v) and np.isnan(want[k])) or v == want[k], k
     n = want.size
     assert stats.true_median_rel_error(g, e, n) == 0.5 * (want[n // 2 - 1] + want[n // 2])
+    # Errors that nearly all share their top digits (and many exactly equal):
+    # whole warps add to one histogram bin at once.
+    rs = np.random.default_rng(2)
+    exact = rs.standard_normal(300_001)
+    got = exact * (1 + 2.0 ** -10)
+    got[::3] = exact[::3] * (1 + 2.0 ** -11)
+    want = java_sorted_rel(got, exact)
+    g, e = torch.from_numpy(got).cuda(), torch.from_numpy(exact).cuda()
+    for k in [0, 99_999, 100_000, 100_001, 150_000, want.size - 1]:
+        assert stats.kth_rel_error(g, e, k) == want[k], k
 
 
 def _free_port():
