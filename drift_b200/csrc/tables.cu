@@ -1,12 +1,12 @@
 // tables.cu — the format tables of DumpTables, written by the device codec.
 //
 // DumpTables (java/src/main/java/io/drift/tools/DumpTables.java:61-124)
-// writes what the formats believe so an independent exact-rational checker
-// can recompute it: the value of every code, and the nearest-even code of
+// writes what the formats believe so an independent exact-rational
+// verification can recompute it: the value of every code, and the nearest-even code of
 // the product and of the sum of code pairs, every ordered pair for formats
 // up to 8 bits and a fixed Rng sample for the 16-bit ones. These kernels
 // produce the same rows from the same device encode/decode the casts use, so
-// the checker covers the engine's codec directly.
+// that verification covers the engine's codec directly.
 #include "codec.cuh"
 #include "internal.h"
 

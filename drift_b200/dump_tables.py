@@ -1,4 +1,4 @@
-"""DumpTables on the device: the format tables an exact-rational checker reads.
+"""DumpTables on the device: the format tables an exact-rational verification reads.
 
 Mirrors io.drift.tools.DumpTables (java/src/main/java/io/drift/tools/DumpTables.java)
 file for file: for every format of Formats.ALL a ``values_<name>.csv`` with the

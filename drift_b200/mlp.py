@@ -10,7 +10,7 @@ cross-entropy stay in double on the host, as the reference keeps them
 per layer per step, Pass.java:249-271).
 
 The arithmetic backend is pluggable so that the same pass can be run on the
-engine and on a checker with identical host code; the engine's backend is the
+engine and on a CPU restatement with identical host code; the engine's backend is the
 default and the only one in this package.
 """
 from __future__ import annotations

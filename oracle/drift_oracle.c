@@ -1,7 +1,7 @@
 /*
  * drift_oracle.c — CPU restatement of drift's emulated-matmul arithmetic.
  *
- * TEST INFRASTRUCTURE ONLY: the checker for the CUDA engine. Only the tests,
+ * TEST INFRASTRUCTURE ONLY: the oracle for the CUDA engine. Only the tests,
  * the smoke check and the benchmark's CPU-baseline leg load it.
  *
  * Every function follows the Java source line by line (IEEE binary64, round

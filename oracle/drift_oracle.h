@@ -1,7 +1,7 @@
 /*
  * drift_oracle.h — CPU restatement of drift's emulated-matmul arithmetic.
  *
- * TEST INFRASTRUCTURE ONLY. This is the checker the CUDA engine is compared
+ * TEST INFRASTRUCTURE ONLY. This is the oracle the CUDA engine is compared
  * against (tests, smoke check, and the CPU-baseline leg of the benchmark). No
  * product code links, loads or calls it.
  *

@@ -1,6 +1,6 @@
 """ctypes front end of the CPU oracle (liboracle.so).
 
-TEST INFRASTRUCTURE ONLY: the checker the CUDA engine is compared against.
+TEST INFRASTRUCTURE ONLY: the oracle the CUDA engine is compared against.
 Only tests/, the smoke check and bench.py's CPU-baseline leg import this
 module. It restates the reference's Java arithmetic in C; see
 drift_oracle.c for the line-by-line citations.

@@ -54,7 +54,7 @@ def opolicy(p):
 
 
 class OracleBackend:
-    """Casts and contractions on the oracle, for the checker's pass of the
+    """Casts and contractions on the oracle, for the oracle's pass of the
     training-step mirrors (drift_b200.mlp, drift_b200.attn)."""
 
     name = "oracle"
