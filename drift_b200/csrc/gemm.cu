@@ -99,15 +99,15 @@ enum SegMode { SEG_NONE = 0, SEG_TILE = 1, SEG_SCHED = 2 };
 // back, step_cvt), the int_cols columns before it on the integer pipes
 // (step_int), the rest on the FP64 pipe (step). Splitting the rounding lifts
 // the FP64 pipe's share below four operations per MAC. Measured at 8192^3 on
-// one B200, one integer column and the conversion column against every
-// column on the FP64 pipe: FP32 sequential +8.6%, pairwise +5.3%, blocked
-// +7.7%; BF16 sequential +7.9%, pairwise +5.2%, blocked +5.7%; two integer
-// columns: FP32 sequential and blocked another +1.9% and +1.0%, BF16
-// sequential and blocked -2.6% and -3.4%. (The
-// conversion column alone: FP32 pairwise +3.2%, BF16 pairwise +2.7%,
-// blocked +1.0%; integer columns alone, one / two: FP32 sequential +5.1% /
-// +6.3%, BF16 sequential +2.5% / +5.0%. Two conversion columns saturate that
-// pipe: FP32 sequential +0.6%.)
+// one B200 against every column on the FP64 pipe:
+//   conversion column + one integer column: FP32 sequential +8.6%, pairwise
+//     +5.3%, blocked +7.7%; BF16 sequential +7.9%, pairwise +5.2%, blocked
+//     +5.7%;
+//   + a second integer column: FP32 sequential and blocked another +1.9% and
+//     +1.0%, BF16 sequential and blocked -2.6% and -3.4% (so FP32 only);
+//   integer columns alone, one / two: FP32 sequential +5.1% / +6.3%, BF16
+//     sequential +2.5% / +5.0%;
+//   two conversion columns saturate that pipe: FP32 sequential +0.6%.
 template <int ACC, int RM, bool PROVEN>
 constexpr bool cvt_col() {
     return PROVEN && RM == DRIFT_NEAREST_EVEN && (ACC == DRIFT_ACC_FP32 || ACC == DRIFT_ACC_BF16);
