@@ -386,8 +386,10 @@ def run_engine(args):
     if not args.no_e2e:
         e2e = run_e2e(d, args, A, B, pols, exact_p, world, rank, pg)
 
+    # The host-core baseline is timed at N = 1 only (rank 0); at N > 1 the
+    # line carries none, so no rank waits on it.
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, cores, desc = cpu_baseline(S)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}
 
