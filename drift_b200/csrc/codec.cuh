@@ -203,24 +203,16 @@ __device__ __forceinline__ double acc_round_any(int acc, double x, int rm, uint6
                                  : acc_round_general<DRIFT_ACC_BF16>(x, rm, u53, drew);
 }
 
-// ------------------------------------------------------- fast accumulator rounding
+// ------------------------------------------------------- magic-constant rounding
 //
-// The contraction rounds once per multiply-accumulate, so the common case
-// must be cheap. For a sum t whose rounded value is a normal number of the
-// accumulator format, rounding to nearest even at a fixed number of
-// significand bits is (t + C) - C with C = 1.5 * 2^(e + SHIFT), e the binade
-// of t and SHIFT = 52 - kept fraction bits: the ulp of C is exactly the
-// target quantum, C is an even multiple of it (so ties go to even), and the
-// subtraction is exact. Building C takes two integer ops on the high word;
-// the two adds run on the FP64 pipe. Truncation clears the low bits.
-//
-// The result is then range-checked on the FP32 pipe: the high word read as a
-// float orders like |r|, so two float compares test 2^min_exp <= |r| <
-// 2^(max_exp+1). Anything outside (zero, the target's subnormal range,
-// overflow, Inf, NaN) is recomputed exactly by the caller. A value just below
-// the normal range that the fine rounding lifts to exactly 2^min_exp is also
-// right: the coarser subnormal quantum rounds it there too, so checking the
-// result alone is enough.
+// For a sum t whose rounded value is a normal number of the accumulator
+// format, rounding to nearest even at a fixed number of significand bits is
+// (t + C) - C with C = 1.5 * 2^(e + SHIFT), e the binade of t and SHIFT = 52 -
+// kept fraction bits: the ulp of C is exactly the target quantum, C is an
+// even multiple of it (so ties go to even), and the subtraction is exact.
+// Truncation clears the low bits. The exact FP16/BF16 rounding uses these for
+// its normal range (narrow_exact); the contraction's fast form below builds
+// the same constant more cheaply.
 
 template <int SHIFT>
 __device__ __forceinline__ double rne_shift(double t) {
@@ -239,19 +231,14 @@ __device__ __forceinline__ double trunc_shift(double t) {
     }
 }
 
-// lo_e <= biased exponent of r < hi_e, read from the high word on the FP32 pipe.
-template <int LO_E, int HI_E>
-__device__ __forceinline__ bool exp_in_range(double r) {
-    const float f = fabsf(__int_as_float(__double2hiint(r)));
-    return f >= __int_as_float(LO_E << 20) && f < __int_as_float(HI_E << 20);
-}
-
-// ------------------------------------------------- fast rounding, tiled contraction form
+// ------------------------------------------------- fast rounding (FastForm)
 //
-// The tiled contraction rounds every sum, so its form is the cheapest in
-// issued instructions: one LOP3, two FP64-pipe ops, and a range word per sum
-// that the caller folds into one word per group (a 3-input max takes two
-// sums at a time) and checks once.
+// Every contraction rounds every sum, so this form is the cheapest in issued
+// instructions: one LOP3, two FP64-pipe ops, and a range word per sum that
+// the caller folds into one word per group (a 3-input max takes two sums at
+// a time) and checks once. The tiled kernel checks groups of a thread's
+// outputs; the one-output-per-thread kernels check eight steps of a chain, or
+// each step.
 //
 // With e the binade of t and D = 1.5 * 2^e, C = D * 2^SHIFT is the magic
 // constant of rne_shift, and fma(D, 2^SHIFT, t) = RN(t + C); fma(D, -2^SHIFT,
@@ -329,8 +316,6 @@ struct FastForm {
 //   step_int(t, r)         the same rounding on the integer pipes;
 //   fold2(run, r0, r1)     folds two range words into a group's word;
 //   valid(run)             whether every step folded into run was exact;
-//   fast(t) / ok(r)        the older rne_shift form with a range check on the
-//                          rounded value (per-thread chains);
 //   exact(t)               any input.
 template <int ACC, int RM> struct AccRound;
 
@@ -339,8 +324,6 @@ template <int RM> struct AccRound<DRIFT_ACC_FP64, RM> {
     __device__ static double step_int(double t, unsigned &) { return t; }
     __device__ static unsigned fold2(unsigned run, unsigned, unsigned) { return run; }
     __device__ static bool valid(unsigned) { return true; }
-    __device__ static double fast(double t) { return t; }
-    __device__ static bool ok(double) { return true; }
     __device__ static double exact(double t) { return t; }
 };
 
@@ -357,8 +340,6 @@ template <int RM> struct AccRound<DRIFT_ACC_FP32, RM> {
         return Fast::fold2(run, r0, r1);
     }
     __device__ static bool valid(unsigned run) { return Fast::valid(run); }
-    __device__ static double fast(double t) { return rne_shift<29>(t); }
-    __device__ static bool ok(double r) { return exp_in_range<1023 - 126, 1023 + 128>(r); }
     __device__ static double exact(double t) { return (double)__double2float_rn(t); }
 };
 
@@ -398,12 +379,6 @@ template <int RM> struct AccRound<DRIFT_ACC_FP16, RM> {
         return Fast::fold2(run, r0, r1);
     }
     __device__ static bool valid(unsigned run) { return Fast::valid(run); }
-    __device__ static double fast(double t) {
-        return RM == DRIFT_TRUNCATE ? trunc_shift<52 - F::mant>(t) : rne_shift<52 - F::mant>(t);
-    }
-    __device__ static bool ok(double r) {
-        return exp_in_range<1023 + F::min_exp, 1023 + F::max_exp + 1>(r);
-    }
     __device__ static double exact(double t) { return narrow_exact<DRIFT_ACC_FP16, RM>(t); }
 };
 
@@ -426,12 +401,6 @@ template <int RM> struct AccRound<DRIFT_ACC_BF16, RM> {
         return Fast::fold2(run, r0, r1);
     }
     __device__ static bool valid(unsigned run) { return Fast::valid(run); }
-    __device__ static double fast(double t) {
-        return RM == DRIFT_TRUNCATE ? trunc_shift<52 - F::mant>(t) : rne_shift<52 - F::mant>(t);
-    }
-    __device__ static bool ok(double r) {
-        return exp_in_range<1023 + F::min_exp, 1023 + F::max_exp + 1>(r);
-    }
     __device__ static double exact(double t) { return narrow_exact<DRIFT_ACC_BF16, RM>(t); }
 };
 

@@ -129,11 +129,15 @@ __device__ __forceinline__ double sr_round(double x, uint64_t &z, uint32_t &cnt)
 // FP64, (float) for FP32, Dot.round for FP16/BF16.
 template <int ACC, int RM> struct ExactRounder {
     __device__ double operator()(double t) {
-        // The contraction kernel's fast rounding, checked; the exact form
-        // only when the result leaves the accumulator's normal range.
+        // The contraction kernel's fast rounding (FastForm), checked on the
+        // sum's range word; the exact form only when the sum lies outside
+        // the accumulator's normal range below its top binade. The low word
+        // of the magic constant is zero here (any accumulator value's low
+        // word keeps the rounding exact; zero is one).
         using R = AccRound<ACC, RM>;
-        const double r = R::fast(t);
-        return R::ok(r) ? r : R::exact(t);
+        unsigned u;
+        const double r = R::step(t, 0, u);
+        return R::valid(R::fold2(0u, u, u)) ? r : R::exact(t);
     }
 };
 
@@ -505,13 +509,13 @@ __global__ void __launch_bounds__(kStageSide *kStageSide, 4)
                 } else {
                     using R = AccRound<ACC, RM>;
                     const double s0 = acc;
-                    bool ok = true;
+                    unsigned run = 0, u[8];
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        acc = R::fast(__dadd_rn(acc, pr[j]));
-                        ok = ok & R::ok(acc);
-                    }
-                    if (!ok) {
+                    for (int j = 0; j < 8; j++)
+                        acc = R::step(__dadd_rn(acc, pr[j]), __double2loint(acc), u[j]);
+#pragma unroll
+                    for (int j = 0; j < 8; j += 2) run = R::fold2(run, u[j], u[j + 1]);
+                    if (!R::valid(run)) {
                         acc = s0;
 #pragma unroll
                         for (int j = 0; j < 8; j++) acc = R::exact(__dadd_rn(acc, pr[j]));
