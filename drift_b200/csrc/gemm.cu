@@ -104,7 +104,8 @@ enum SegMode { SEG_NONE = 0, SEG_TILE = 1, SEG_SCHED = 2 };
 //     +5.3%, blocked +7.7%; BF16 sequential +7.9%, pairwise +5.2%, blocked
 //     +5.7%;
 //   + a second integer column: FP32 sequential and blocked another +1.9% and
-//     +1.0%, BF16 sequential and blocked -2.6% and -3.4% (so FP32 only);
+//     +1.0%, FP32 pairwise -1.0%, BF16 sequential and blocked -2.6% and
+//     -3.4% (so FP32 sequential and blocked only);
 //   integer columns alone, one / two: FP32 sequential +5.1% / +6.3%, BF16
 //     sequential +2.5% / +5.0%;
 //   two conversion columns saturate that pipe: FP32 sequential +0.6%.
