@@ -572,6 +572,41 @@ __global__ void __launch_bounds__(kStageSide *kStageSide, 4)
             }
         }
         v = blk ? total : acc;
+    } else if (g.order == DRIFT_PAIRWISE && g.depth >= kStageK &&
+               (g.depth & (g.depth - 1)) == 0) {
+        // Dot.pairwise (:86-102) over a power-of-two depth: every split is
+        // exact and every leaf is 8 long, so each aligned 32-term chunk is a
+        // whole subtree ((leaf0 + leaf1) + (leaf2 + leaf3)), and the chunks
+        // combine as a perfect binary tree: after chunk c, ctz(c + 1) merges
+        // of the pending nodes (left operand first, as the recursion's
+        // post-order gives). One staged chunk at a time, double-buffered as
+        // in the walk above; a thread's pending nodes stay in its own stack.
+        const int64_t nc = g.depth / kStageK;
+        double stk[32];  // log2(nc) + 1 entries; depth < 2^36
+        int sp = 0;
+        __syncthreads();
+        for (int64_t c = 0; c < nc; c++) {
+            fetch(c * kStageK);
+            put(c & 1);  // last read two chunks ago
+            __syncthreads();
+            const double *ra = sA[c & 1][ty], *rb = sB[c & 1][tx];
+            double leaf[4];
+#pragma unroll
+            for (int l = 0; l < 4; l++) {
+                double p[8];
+#pragma unroll
+                for (int j = 0; j < 8; j++) p[j] = __dmul_rn(ra[8 * l + j], rb[8 * l + j]);
+                double sum = 0.0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) sum = rnd(__dadd_rn(sum, p[j]));
+                leaf[l] = sum;
+            }
+            double node = rnd(__dadd_rn(rnd(__dadd_rn(leaf[0], leaf[1])),
+                                        rnd(__dadd_rn(leaf[2], leaf[3]))));
+            for (int64_t m = c + 1; (m & 1) == 0; m >>= 1) node = rnd(__dadd_rn(stk[--sp], node));
+            stk[sp++] = node;
+        }
+        v = stk[0];
     } else {
         // FULL windows only (the launcher sends no other window here).
         auto term = [&](int64_t k) {
